@@ -1,0 +1,49 @@
+// Shared device/host helpers for libb2o (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+namespace b2o {
+
+// ---------------------------------------------------------------- status ---
+// Host-side error text for the last failing call on this thread.
+void set_error(const std::string& msg);
+// Counts kernel launches made by the library (reported by the benchmark).
+extern std::atomic<int64_t> g_launches;
+inline void count_launch(int n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Device error word (one per device, lazily allocated by the library at load
+// of the first device call; see c_abi.cu). Kernels OR error bits into it.
+int* device_error_word();
+
+enum DeviceError : int {
+  kErrWaitTimeout = 1,     // a bounded mbarrier wait ran out
+  kErrBadTile = 2,         // a tile index outside the problem (never expected)
+};
+
+// Returns 0 or the CUDA error of the last launch (and records the message).
+int check_launch(const char* what);
+
+// ------------------------------------------------------------- numerics ---
+// bf16 <-> fp32 with round-to-nearest-even (the rounding torch uses for
+// .to(torch.bfloat16) and for bf16 tensor arithmetic).
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// torch's lerp (ATen/native/Lerp.h): small weights interpolate from `self`,
+// large ones from `end`; evaluated in fp32 opmath with fused multiply-add.
+__device__ __forceinline__ float torch_lerp(float self, float end, float w) {
+  return (fabsf(w) < 0.5f) ? fmaf(w, end - self, self) : fmaf(-(end - self), 1.0f - w, end);
+}
+
+}  // namespace b2o

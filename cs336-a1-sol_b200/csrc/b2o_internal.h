@@ -1,0 +1,61 @@
+// Internal (C++) interfaces shared by the translation units of libb2o.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b2o.h"
+
+namespace b2o {
+
+int num_sms();
+
+// ---- streaming.cu
+int adamw_step(const b2o_adamw_tensor* tensors, int ntensors, const b2o_adamw_group* groups,
+               int ngroups, int param_dtype, int state_dtype, float ema_weight, cudaStream_t stream);
+int ema_update(float* const* shadows, const void* const* params, const int64_t* numels, int nt,
+               int param_dtype, float w, cudaStream_t stream);
+int ema_copy_to_params(const float* const* shadows, void* const* params, const int64_t* numels, int nt,
+                       int param_dtype, cudaStream_t stream);
+int normuon_front_parts(int64_t rc);
+int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int c, int dtype,
+                  float w_small, float w_large, int nesterov, uint16_t* U, float* partial,
+                  cudaStream_t stream);
+int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
+                  uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
+                  float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
+                  float w_beta2, float ema_weight, float* scratch, cudaStream_t stream);
+
+// ---- gemm.cu
+// Operand view: element (row i, k) of an op(A) that is M x K (or op(B) that is N x K).
+struct Operand {
+  const uint16_t* ptr;
+  int64_t ld;       // elements between consecutive stored rows
+  int64_t stride;   // elements between batch entries
+  int kmajor;       // 1: stored [i][k] (k contiguous); 0: stored [k][i] (i contiguous)
+};
+struct Epilogue {
+  int kind;          // 0 scale, 1 poly (alpha*I + beta*C + gamma*acc), 2 quintic-B, 3 quintic-X
+  float alpha, beta, gamma;
+  const float* scale;  // per-batch factor on acc (kind 0), may be null
+  const uint16_t* C;   // addend (kinds 1..3)
+  int64_t ldc, strideC;
+  uint16_t* D;
+  int64_t ldd, strideD;
+  float* rowsq;        // per-row partial sums of bf16(D)^2: [b][tile_n (256 wide)][M]
+};
+int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch,
+         int sym, cudaStream_t stream);
+// Forces the CUDA-core path (tests compare both paths).
+int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch,
+              cudaStream_t stream);
+bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K);
+
+// ---- ortho.cu
+int64_t ortho_workspace_bytes(int S, int r, int c);
+int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode,
+                  const float* coeffs, int T, const int* resets, int nresets, float norm_eps,
+                  float norm_safety, void* ws, int64_t ws_bytes, uint16_t* out, float* rowsq,
+                  cudaStream_t stream);
+
+}  // namespace b2o

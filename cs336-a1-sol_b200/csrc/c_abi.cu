@@ -1,0 +1,172 @@
+// extern "C" entry points of libb2o (declared in include/b2o.h) and the
+// library-wide plumbing: error text, launch counter, device error word.
+#include "b2o_common.cuh"
+#include "b2o_internal.h"
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+namespace b2o {
+
+std::atomic<int64_t> g_launches{0};
+static thread_local std::string t_last_error;
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return static_cast<int>(e);
+  }
+  return 0;
+}
+
+// The device error word lives in statically allocated device memory (no
+// cudaMalloc); kernels receive its address as an argument.
+__device__ int g_device_error;
+
+constexpr int kMaxDevices = 64;
+static int* g_err_ptr[kMaxDevices];
+static int g_sms[kMaxDevices];
+static std::mutex g_mu;
+
+int* device_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_err_ptr[dev];
+}
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sms[dev] = n;
+  }
+  return g_sms[dev];
+}
+
+}  // namespace b2o
+
+using namespace b2o;
+
+extern "C" {
+
+int b2o_version(void) { return 1; }
+
+int b2o_last_error(char* buf, int buflen) {
+  if (!buf || buflen <= 0) return static_cast<int>(t_last_error.size());
+  const int n = std::min<int>(buflen - 1, static_cast<int>(t_last_error.size()));
+  memcpy(buf, t_last_error.data(), n);
+  buf[n] = 0;
+  return n;
+}
+
+int64_t b2o_launch_count(void) { return g_launches.load(); }
+
+int b2o_num_sms(void) { return num_sms(); }
+
+int b2o_check_device_error(void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) { set_error(std::string("sync: ") + cudaGetErrorString(e)); return -static_cast<int>(e); }
+  int* w = device_error_word();
+  if (!w) { set_error("no device error word"); return -1; }
+  int val = 0;
+  e = cudaMemcpyAsync(&val, w, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) { set_error(std::string("read error word: ") + cudaGetErrorString(e)); return -static_cast<int>(e); }
+  if (val) {
+    const int zero = 0;
+    cudaMemcpyAsync(w, &zero, sizeof(int), cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+    set_error("device error word = " + std::to_string(val));
+  }
+  return val;
+}
+
+int b2o_adamw_step(const b2o_adamw_tensor* tensors, int ntensors, const b2o_adamw_group* groups, int ngroups,
+                   int param_dtype, int state_dtype, float ema_weight, void* stream) {
+  return adamw_step(tensors, ntensors, groups, ngroups, param_dtype, state_dtype, ema_weight,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int b2o_ema_update(float* const* shadows, const void* const* params, const int64_t* numels, int ntensors,
+                   int param_dtype, float weight, void* stream) {
+  return ema_update(shadows, params, numels, ntensors, param_dtype, weight, static_cast<cudaStream_t>(stream));
+}
+
+int b2o_ema_copy_to_params(const float* const* shadows, void* const* params, const int64_t* numels, int ntensors,
+                           int param_dtype, void* stream) {
+  return ema_copy_to_params(shadows, params, numels, ntensors, param_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int b2o_normuon_front_parts(int64_t rc) { return normuon_front_parts(rc); }
+
+int b2o_normuon_front(const void* const* d_grads, void* const* d_bufs, int S, int r, int c, int dtype,
+                      float w_small, float w_large, int nesterov, uint16_t* d_u, float* d_partial, void* stream) {
+  return normuon_front(d_grads, d_bufs, S, r, c, dtype, w_small, w_large, nesterov, d_u, d_partial,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int64_t b2o_ortho_workspace_bytes(int S, int r, int c) { return ortho_workspace_bytes(S, r, c); }
+
+int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r, int c, int mode,
+                      const float* coeffs, int T, const int* resets, int nresets, float norm_eps, float norm_safety,
+                      void* d_ws, int64_t ws_bytes, uint16_t* d_out, float* d_rowsq, void* stream) {
+  return orthogonalize(d_u, d_partial, S, r, c, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, d_ws,
+                       ws_bytes, d_out, d_rowsq, static_cast<cudaStream_t>(stream));
+}
+
+int64_t b2o_normuon_apply_scratch_floats(int S, int r) {
+  return static_cast<int64_t>(S) * (r + 4);
+}
+
+int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c, void* const* params,
+                      uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype, float neg_lr,
+                      float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale, float w_beta2,
+                      float ema_weight, float* d_scratch, void* stream) {
+  return normuon_apply(d_o, d_rowsq, S, r, c, params, rems, emas, vrows, param_dtype, neg_lr, lr_wd, wd_factor,
+                       wd_on, cautious, shape_scale, w_beta2, ema_weight, d_scratch,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int b2o_gemm_bf16(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B, int64_t ldb,
+                  int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD, const uint16_t* d_C,
+                  int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int epi, int sym, float alpha,
+                  float beta, float gamma, const float* d_scale, float* d_rowsq, void* stream) {
+  Operand A{d_A, lda, strideA, a_kmajor ? 1 : 0};
+  Operand B{d_B, ldb, strideB, b_kmajor ? 1 : 0};
+  Epilogue e;
+  memset(&e, 0, sizeof(e));
+  e.kind = epi; e.alpha = alpha; e.beta = beta; e.gamma = gamma; e.scale = d_scale;
+  e.C = d_C; e.ldc = ldc; e.strideC = strideC; e.D = d_D; e.ldd = ldd; e.strideD = strideD; e.rowsq = d_rowsq;
+  return gemm(A, B, e, M, N, K, batch, sym, static_cast<cudaStream_t>(stream));
+}
+
+/* Test hook: the same GEMM on the CUDA-core path (no tensor cores). */
+int b2o_gemm_bf16_simt(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B,
+                       int64_t ldb, int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD,
+                       const uint16_t* d_C, int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int epi,
+                       float alpha, float beta, float gamma, const float* d_scale, float* d_rowsq, void* stream) {
+  Operand A{d_A, lda, strideA, a_kmajor ? 1 : 0};
+  Operand B{d_B, ldb, strideB, b_kmajor ? 1 : 0};
+  Epilogue e;
+  memset(&e, 0, sizeof(e));
+  e.kind = epi; e.alpha = alpha; e.beta = beta; e.gamma = gamma; e.scale = d_scale;
+  e.C = d_C; e.ldc = ldc; e.strideC = strideC; e.D = d_D; e.ldd = ldd; e.strideD = strideD; e.rowsq = d_rowsq;
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !d_A || !d_B || !d_D) { set_error("gemm_simt: bad args"); return -1; }
+  return gemm_simt(A, B, e, M, N, K, batch, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,572 @@
+// Batched bf16 GEMM for the Newton-Schulz orthogonaliser, written for sm_100a:
+//   * tcgen05.mma (cta_group::1, kind::f16, M=128 N=256 K=16) accumulating fp32
+//     in tensor memory, two 256-column accumulators so the epilogue of one tile
+//     overlaps the main loop of the next;
+//   * operands staged by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
+//     multicast) through a 4-stage mbarrier ring; either operand may be K-major
+//     or MN-major, so tall matrices are consumed in their stored layout;
+//   * a persistent grid (one CTA per SM) walking a static tile schedule;
+//     symmetric outputs compute only tiles that touch the upper triangle and
+//     mirror them in the epilogue;
+//   * warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (and TMEM owner),
+//     warps 2-5 = epilogue (one TMEM lane quadrant each).
+// Every wait is bounded: on expiry the CTA raises the device error word,
+// drains its own copies and MMAs (again bounded), frees TMEM and returns.
+// A CUDA-core kernel covers shapes the tensor-core path does not take
+// (min(M,N) < 128, unaligned strides) with the same epilogues.
+#include "b2o_common.cuh"
+#include "b2o_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+namespace b2o {
+
+namespace tc {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 columns
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+struct Params {
+  int M, N, K, batch;
+  int a_kmajor, b_kmajor, sym;
+  int tiles_m, tiles_n, tiles_per_batch, total_tiles, nk;
+  Epilogue e;
+  int* err;
+};
+
+// ------------------------------------------------------------ PTX helpers --
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait. Returns false when the CTA is aborting (this wait ran out or
+// another role of the CTA gave up).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// 128-byte-swizzled shared-memory matrix descriptor (sm_100 layout: start
+// address, leading/stride byte offsets, version 1, layout type 2 = SW128).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* out) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) out[i] = __uint_as_float(r[i]);
+}
+
+// Tile t of the schedule -> (batch, tile_m, tile_n). Symmetric outputs keep
+// the tiles whose column range reaches the diagonal block of their rows.
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_batch;
+  int local = t - b * p.tiles_per_batch;
+  if (!p.sym) {
+    tn = local / p.tiles_m;   // consecutive CTAs share the B column block
+    tm = local - tn * p.tiles_m;
+    return;
+  }
+  tn = 0;
+  while (true) {
+    const int cnt = min(p.tiles_m, (tn * BN + BN - 1) / BM + 1);
+    if (local < cnt) { tm = local; return; }
+    local -= cnt;
+    ++tn;
+  }
+}
+
+// ----------------------------------------------------------- epilogue ------
+__device__ __forceinline__ void load_row32(const uint16_t* base, int64_t ld, int row, int col0, int M, int N,
+                                           bool vec, float* out) {
+  if (vec) {
+    const uint4* src = reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row) * ld + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 v = src[q];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        out[q * 8 + 2 * h] = bf16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu));
+        out[q * 8 + 2 * h + 1] = bf16_to_f32(static_cast<uint16_t>(w[h] >> 16));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int col = col0 + j;
+      out[j] = (row < M && col < N) ? bf16_to_f32(base[static_cast<int64_t>(row) * ld + col]) : 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ float epi_value(const Params& p, int kind, float acc, float c, float sc, int row,
+                                           int col) {
+  switch (kind) {
+    case 0:
+      return acc * sc;
+    case 1:
+      return fmaf(p.e.gamma, acc, fmaf(p.e.beta, c, row == col ? p.e.alpha : 0.f));
+    case 2:
+      return round_bf16(round_bf16(p.e.beta * c) + round_bf16(p.e.gamma * round_bf16(acc)));
+    default:
+      return round_bf16(round_bf16(p.e.alpha * c) + round_bf16(acc));
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 128); }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_phase[STAGES];  // phase of the last load issued into each stage
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        int b, tm, tn;
+        tile_coords(p, t, b, tm, tn);
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t a_dst = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_dst = a_dst + A_BYTES;
+          mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
+          if (p.a_kmajor) {
+            tma_load_3d(a_dst, &tmA, kb * BK, tm * BM, b, &full_bar[stage]);
+          } else {
+            tma_load_3d(a_dst, &tmA, tm * BM, kb * BK, b, &full_bar[stage]);
+            tma_load_3d(a_dst + 8192, &tmA, tm * BM + 64, kb * BK, b, &full_bar[stage]);
+          }
+          if (p.b_kmajor) {
+            tma_load_3d(b_dst, &tmB, kb * BK, tn * BN, b, &full_bar[stage]);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tma_load_3d(b_dst + q * 8192, &tmB, tn * BN + q * 64, kb * BK, b, &full_bar[stage]);
+          }
+          last_phase[stage] = static_cast<int>(phase);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Drain: wait (bounded) until the last load issued into each stage has
+        // landed, so no copy into this CTA's shared memory outlives it.
+        const uint64_t t0 = globaltimer();
+        for (int s = 0; s < STAGES; ++s) {
+          if (last_phase[s] < 0) continue;
+          while (!mbar_try_wait(&full_bar[s], static_cast<uint32_t>(last_phase[s]))) {
+            if (globaltimer() - t0 > kTimeoutNs) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer ---
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(!p.a_kmajor) << 15) |
+                             (static_cast<uint32_t>(!p.b_kmajor) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                             (static_cast<uint32_t>(BM >> 4) << 24);
+      const uint32_t a_lbo = p.a_kmajor ? 16u : 8192u;
+      const uint32_t b_lbo = p.b_kmajor ? 16u : 8192u;
+      const uint32_t a_kstep = p.a_kmajor ? 32u : 2048u;
+      const uint32_t b_kstep = p.b_kmajor ? 32u : 2048u;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
+        fence_after_sync();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          fence_after_sync();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = make_desc(a_addr + kk * a_kstep, a_lbo, 1024u);
+            const uint64_t bd = make_desc(b_addr + kk * b_kstep, b_lbo, 1024u);
+            mma_bf16(tmem_d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);  // frees the stage once these MMAs retire
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar[acc]);      // accumulator ready for the epilogue
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is freed.
+      mma_commit(drain_bar);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain_bar, 0)) {
+        if (globaltimer() - t0 > kTimeoutNs) { *abort_flag = 1; break; }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue ---
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
+    int local = 0;
+    const Epilogue& e = p.e;
+    const bool vec_d = ((e.ldd & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.D) & 15) == 0) &&
+                       ((e.strideD & 7) == 0);
+    const bool vec_c = e.C && ((e.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.C) & 15) == 0) &&
+                       ((e.strideC & 7) == 0);
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++local) {
+      int b, tm, tn;
+      tile_coords(p, t, b, tm, tn);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag)) break;
+      fence_after_sync();
+      const int row = tm * BM + quad * 32 + lane;
+      const float sc = e.scale ? e.alpha * e.scale[b] : e.alpha;
+      uint16_t* Db = e.D + static_cast<int64_t>(b) * e.strideD;
+      const uint16_t* Cb = e.C ? e.C + static_cast<int64_t>(b) * e.strideC : nullptr;
+      float rsq = 0.f;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
+        const int col0 = tn * BN + ch * 32;
+        if (col0 < p.N && row < p.M) {
+          const bool full = col0 + 32 <= p.N;
+          float cv[32];
+          if (e.kind != 0) load_row32(Cb, e.ldc, row, col0, p.M, p.N, vec_c && full, cv);
+          uint16_t out[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = epi_value(p, e.kind, v[j], e.kind != 0 ? cv[j] : 0.f, sc, row, col0 + j);
+            out[j] = f32_to_bf16(x);
+            const float xr = bf16_to_f32(out[j]);
+            if (col0 + j < p.N) rsq = fmaf(xr, xr, rsq);
+          }
+          if (!p.sym) {
+            if (full && vec_d) {
+              uint4* dst = reinterpret_cast<uint4*>(Db + static_cast<int64_t>(row) * e.ldd + col0);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 w;
+                w.x = out[q * 8 + 0] | (static_cast<uint32_t>(out[q * 8 + 1]) << 16);
+                w.y = out[q * 8 + 2] | (static_cast<uint32_t>(out[q * 8 + 3]) << 16);
+                w.z = out[q * 8 + 4] | (static_cast<uint32_t>(out[q * 8 + 5]) << 16);
+                w.w = out[q * 8 + 6] | (static_cast<uint32_t>(out[q * 8 + 7]) << 16);
+                dst[q] = w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) Db[static_cast<int64_t>(row) * e.ldd + col0 + j] = out[j];
+            }
+          } else {
+            // symmetric: keep col >= row, write it and its mirror
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = col0 + j;
+              if (col < p.N && col >= row) {
+                Db[static_cast<int64_t>(row) * e.ldd + col] = out[j];
+                Db[static_cast<int64_t>(col) * e.ldd + row] = out[j];
+              }
+            }
+          }
+        }
+      }
+      fence_before_sync();
+      mbar_arrive(&tempty_bar[acc]);
+      if (e.rowsq && row < p.M)
+        e.rowsq[(static_cast<int64_t>(b) * p.tiles_n + tn) * p.M + row] = rsq;
+    }
+  }
+
+  fence_before_sync();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(p.err, kErrWaitTimeout);
+  if (warp == 1) {
+    __syncwarp();
+    fence_after_sync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------ host-side setup ---
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// rows_box: MN extent of one box for K-major operands (128 for A, 256 for B).
+static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batch, int rows_box) {
+  auto fn = encode_fn();
+  if (!fn) { set_error("gemm: cuTensorMapEncodeTiled unavailable"); return -1; }
+  cuuint64_t dims[3];
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld) * 2, static_cast<cuuint64_t>(op.stride) * 2};
+  cuuint32_t box[3];
+  cuuint32_t estr[3] = {1, 1, 1};
+  if (op.kmajor) {
+    dims[0] = K; dims[1] = mn; box[0] = BK; box[1] = rows_box;
+  } else {
+    dims[0] = mn; dims[1] = K; box[0] = 64; box[1] = BK;
+  }
+  dims[2] = batch; box[2] = 1;
+  if (batch == 1) strides[1] = strides[0] * dims[1];  // any valid stride
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(op.ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm: cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
+    return -1;
+  }
+  return 0;
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------- CUDA cores --
+// One CTA computes a 256-column row segment of one output row.
+__global__ void __launch_bounds__(256) gemm_simt_kernel(Operand A, Operand B, Epilogue E, int M, int N, int K) {
+  const int tn = blockIdx.x, row = blockIdx.y, b = blockIdx.z;
+  const int col = tn * 256 + threadIdx.x;
+  const uint16_t* Ab = A.ptr + static_cast<int64_t>(b) * A.stride;
+  const uint16_t* Bb = B.ptr + static_cast<int64_t>(b) * B.stride;
+  float acc = 0.f;
+  if (col < N) {
+    for (int k = 0; k < K; ++k) {
+      const float a = bf16_to_f32(A.kmajor ? Ab[static_cast<int64_t>(row) * A.ld + k] : Ab[static_cast<int64_t>(k) * A.ld + row]);
+      const float bb = bf16_to_f32(B.kmajor ? Bb[static_cast<int64_t>(col) * B.ld + k] : Bb[static_cast<int64_t>(k) * B.ld + col]);
+      acc = fmaf(a, bb, acc);
+    }
+  }
+  float sq = 0.f;
+  if (col < N) {
+    const float c = E.C ? bf16_to_f32(E.C[static_cast<int64_t>(b) * E.strideC + static_cast<int64_t>(row) * E.ldc + col]) : 0.f;
+    float x;
+    switch (E.kind) {
+      case 0: x = acc * (E.scale ? E.alpha * E.scale[b] : E.alpha); break;
+      case 1: x = fmaf(E.gamma, acc, fmaf(E.beta, c, row == col ? E.alpha : 0.f)); break;
+      case 2: x = round_bf16(round_bf16(E.beta * c) + round_bf16(E.gamma * round_bf16(acc))); break;
+      default: x = round_bf16(round_bf16(E.alpha * c) + round_bf16(acc)); break;
+    }
+    const uint16_t o = f32_to_bf16(x);
+    E.D[static_cast<int64_t>(b) * E.strideD + static_cast<int64_t>(row) * E.ldd + col] = o;
+    const float xr = bf16_to_f32(o);
+    sq = xr * xr;
+  }
+  if (E.rowsq) {
+    __shared__ float red[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < 8; ++w) t += red[w];
+      const int tiles_n = (N + 255) / 256;
+      E.rowsq[(static_cast<int64_t>(b) * tiles_n + tn) * M + row] = t;
+    }
+  }
+}
+
+int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch,
+              cudaStream_t stream) {
+  dim3 grid((N + 255) / 256, M, batch);
+  if (grid.y > 65535u || grid.z > 65535u) { set_error("gemm_simt: problem too large"); return -1; }
+  gemm_simt_kernel<<<grid, 256, 0, stream>>>(A, B, E, M, N, K);
+  count_launch();
+  return check_launch("gemm_simt");
+}
+
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K) {
+  (void)E;
+  if (M < tc::BM || N < 128 || K < tc::BK) return false;
+  if (!al16(A.ptr) || !al16(B.ptr)) return false;
+  if ((A.ld & 7) || (B.ld & 7) || (A.stride & 7) || (B.stride & 7)) return false;
+  return true;
+}
+
+int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch, int sym,
+         cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) { set_error("gemm: empty problem"); return -1; }
+  if (!A.ptr || !B.ptr || !E.D) { set_error("gemm: null operand"); return -1; }
+  if (E.kind < 0 || E.kind > 3) { set_error("gemm: bad epilogue"); return -1; }
+  if (E.kind != 0 && !E.C) { set_error("gemm: epilogue needs C"); return -1; }
+  if (sym && M != N) { set_error("gemm: symmetric output needs M == N"); return -1; }
+  if (sym && E.rowsq) { set_error("gemm: row sums are not produced for symmetric outputs"); return -1; }
+  if (!gemm_tc_supported(A, B, E, M, N, K)) return gemm_simt(A, B, E, M, N, K, batch, stream);
+
+  tc::Params p;
+  memset(&p, 0, sizeof(p));
+  p.M = M; p.N = N; p.K = K; p.batch = batch;
+  p.a_kmajor = A.kmajor; p.b_kmajor = B.kmajor; p.sym = sym;
+  p.tiles_m = (M + tc::BM - 1) / tc::BM;
+  p.tiles_n = (N + tc::BN - 1) / tc::BN;
+  if (sym) {
+    int cnt = 0;
+    for (int tn = 0; tn < p.tiles_n; ++tn) cnt += std::min(p.tiles_m, (tn * tc::BN + tc::BN - 1) / tc::BM + 1);
+    p.tiles_per_batch = cnt;
+  } else {
+    p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  }
+  const int64_t total = static_cast<int64_t>(p.tiles_per_batch) * batch;
+  if (total > (1ll << 30)) { set_error("gemm: too many tiles"); return -1; }
+  p.total_tiles = static_cast<int>(total);
+  p.nk = (K + tc::BK - 1) / tc::BK;
+  p.e = E;
+  p.err = device_error_word();
+  if (!p.err) { set_error("gemm: no device error word"); return -1; }
+
+  CUtensorMap ma, mb;
+  if (tc::make_map(&ma, A, M, K, batch, tc::BM)) return -1;
+  if (tc::make_map(&mb, B, N, K, batch, tc::BN)) return -1;
+
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t ce = cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          tc::SMEM_BYTES);
+    if (ce != cudaSuccess) { set_error(std::string("gemm: smem attribute: ") + cudaGetErrorString(ce)); return ce; }
+    configured_dev = dev;
+  }
+  const int grid = std::min(p.total_tiles, num_sms());
+  tc::gemm_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, p);
+  count_launch();
+  return check_launch("gemm_tc");
+}
+
+}  // namespace b2o

@@ -1,0 +1,251 @@
+// Newton-Schulz orthogonaliser driver for one shape-batch of S matrices (r x c).
+//
+// Reference behaviour: NorMuonGNS._orthogonalize_batch (transformer_lm/sol_modules.py:366-370)
+// calls gram_newton_schulz.GramNewtonSchulz or, when that package is absent, the
+// quintic iteration zeropower_via_newtonschulz5 (sol_modules.py:278-293).
+//
+// Both run on the tcgen05 GEMM of gemm.cu without materialising transposes:
+// a matrix with r > c is iterated as its transpose by switching the operand
+// majorness, and every output is written in the original (r, c) layout.
+//
+//   mode 0 (quintic, the reference's fallback restated):
+//       X0 = bf16(u / bf16(bf16(||u||_F) + eps))
+//       repeat T times:  A = X X^T;  B = bf16(b*A) + bf16(c*bf16(A A));
+//                        X = bf16(a*X) + bf16(B X)          (all bf16 rounded)
+//   mode 1 (Gram Newton-Schulz): iterate on the m x m Gram matrix R = X X^T,
+//       m = min(r, c), with a per-step coefficient table:
+//       P_t = a_t I + b_t R + c_t R^2;  Q <- Q P_t;  R <- P_t R P_t
+//       and form X_T = Q X0 only at restarts and at the end. At a restart step
+//       the iterate X = Q X0 is materialised and R recomputed from it, which
+//       bounds the drift between Q and R accumulated in bf16.
+#include "b2o_common.cuh"
+#include "b2o_internal.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace b2o {
+
+static inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+constexpr int kPool = 6;
+
+struct OrthoLayout {
+  int64_t pool_off, pool_stride, xa_off, xb_off, scal_off, total;
+};
+
+static OrthoLayout layout_for(int S, int r, int c) {
+  const int64_t m = std::min(r, c);
+  OrthoLayout L;
+  L.pool_stride = align_up(static_cast<int64_t>(S) * m * m * 2, 256);
+  L.pool_off = 0;
+  const int64_t xbytes = align_up(static_cast<int64_t>(S) * r * c * 2, 256);
+  L.xa_off = L.pool_off + kPool * L.pool_stride;
+  L.xb_off = L.xa_off + xbytes;
+  L.scal_off = L.xb_off + xbytes;
+  L.total = L.scal_off + align_up(static_cast<int64_t>(4) * S * 4, 256);
+  return L;
+}
+
+int64_t ortho_workspace_bytes(int S, int r, int c) {
+  if (S <= 0 || r <= 0 || c <= 0) return -1;
+  return layout_for(S, r, c).total;
+}
+
+// Per-matrix norm of the front's bf16 output, from its partial sums.
+__global__ void norm_finalize_kernel(const float* __restrict__ partial, int nparts, int S, int mode, float eps,
+                                     float safety, float* __restrict__ scal) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= S) return;
+  float acc = 0.f;
+  for (int i = 0; i < nparts; ++i) acc += partial[static_cast<int64_t>(s) * nparts + i];
+  const float nrm = sqrtf(acc);
+  if (mode == 0) {
+    // X.norm() of a bf16 tensor is returned in bf16; "+ eps" is again bf16 arithmetic
+    const float nb = round_bf16(nrm);
+    scal[2 * S + s] = round_bf16(nb + eps);
+  } else {
+    const float sc = 1.0f / (nrm * safety + eps);
+    scal[s] = sc;
+    scal[S + s] = sc * sc;
+  }
+}
+
+// X0 = bf16(u / d[s]) (the division of zeropower_via_newtonschulz5, sol_modules.py:283).
+__global__ void ns_normalize_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
+                                    const float* __restrict__ div) {
+  const int s = blockIdx.y;
+  const float d = div[s];
+  const uint16_t* u = U + static_cast<int64_t>(s) * rc;
+  uint16_t* x = X + static_cast<int64_t>(s) * rc;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rc;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    x[i] = f32_to_bf16(__fdiv_rn(bf16_to_f32(u[i]), d));
+}
+
+namespace {
+
+struct Batch {
+  int S, r, c, m, n;
+  bool tall;
+  int64_t rc, mm;
+  cudaStream_t st;
+};
+
+// Operand describing the stored (r, c) matrix X as op(X) with rows = m-side.
+// wide (r <= c): X itself; tall: X^T, read MN-major.
+Operand x_as_mk(const Batch& b, const uint16_t* X) {
+  return Operand{X, b.c, b.rc, b.tall ? 0 : 1};
+}
+Operand sq(const Batch& b, const uint16_t* Mx) { return Operand{Mx, b.m, b.mm, 1}; }
+
+Epilogue epi0(uint16_t* D, int64_t ldd, int64_t strideD, float alpha, const float* scale) {
+  Epilogue e;
+  memset(&e, 0, sizeof(e));
+  e.kind = 0; e.alpha = alpha; e.scale = scale; e.D = D; e.ldd = ldd; e.strideD = strideD;
+  return e;
+}
+
+// R = scale * X X^T (m x m, symmetric)
+int syrk(const Batch& b, const uint16_t* X, uint16_t* R, const float* scale) {
+  const Operand A = x_as_mk(b, X);
+  return gemm(A, A, epi0(R, b.m, b.mm, 1.0f, scale), b.m, b.m, b.n, b.S, 1, b.st);
+}
+
+// D (stored r x c) = L X in the m-side frame: wide D = L X, tall D = X L^T.
+int apply_left(const Batch& b, const uint16_t* L, const uint16_t* X, Epilogue e) {
+  e.ldd = b.c; e.strideD = b.rc;
+  if (!b.tall) {
+    const Operand A = sq(b, L);
+    const Operand B{X, b.c, b.rc, 0};  // B[j][k] = X[k][j]
+    return gemm(A, B, e, b.r, b.c, b.m, b.S, 0, b.st);
+  }
+  const Operand A{X, b.c, b.rc, 1};
+  const Operand B = sq(b, L);          // B[j][k] = L[j][k]
+  return gemm(A, B, e, b.r, b.c, b.m, b.S, 0, b.st);
+}
+
+// D = L R^T for m x m operands (R symmetric -> D = L R)
+int prod(const Batch& b, const uint16_t* L, const uint16_t* Rs, Epilogue e, int sym) {
+  e.ldd = b.m; e.strideD = b.mm;
+  return gemm(sq(b, L), sq(b, Rs), e, b.m, b.m, b.m, b.S, sym, b.st);
+}
+
+}  // namespace
+
+int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode, const float* coeffs,
+                  int T, const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
+                  int64_t ws_bytes, uint16_t* out, float* rowsq, cudaStream_t stream) {
+  if (S <= 0 || r <= 0 || c <= 0 || !U || !partial || !ws || !out || !rowsq || !coeffs) {
+    set_error("orthogonalize: bad arguments"); return -1;
+  }
+  if (mode != 0 && mode != 1) { set_error("orthogonalize: mode must be 0 or 1"); return -1; }
+  if (T < 1 || T > 64) { set_error("orthogonalize: 1..64 steps"); return -1; }
+  if (nresets < 0 || (nresets > 0 && !resets)) { set_error("orthogonalize: bad resets"); return -1; }
+  const OrthoLayout L = layout_for(S, r, c);
+  if (ws_bytes < L.total) { set_error("orthogonalize: workspace too small"); return -1; }
+  if (reinterpret_cast<uintptr_t>(ws) & 255) { set_error("orthogonalize: workspace must be 256-byte aligned"); return -1; }
+
+  Batch b;
+  b.S = S; b.r = r; b.c = c; b.m = std::min(r, c); b.n = std::max(r, c); b.tall = r > c;
+  b.rc = static_cast<int64_t>(r) * c; b.mm = static_cast<int64_t>(b.m) * b.m; b.st = stream;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  auto pool = [&](int i) { return reinterpret_cast<uint16_t*>(base + L.pool_off + i * L.pool_stride); };
+  uint16_t* Xa = reinterpret_cast<uint16_t*>(base + L.xa_off);
+  uint16_t* Xb = reinterpret_cast<uint16_t*>(base + L.xb_off);
+  float* scal = reinterpret_cast<float*>(base + L.scal_off);
+
+  const int64_t rc = b.rc;
+  const int nparts = normuon_front_parts(rc);
+  norm_finalize_kernel<<<(S + 127) / 128, 128, 0, stream>>>(partial, nparts, S, mode, norm_eps, norm_safety, scal);
+  count_launch();
+  if (int e = check_launch("norm_finalize")) return e;
+
+  int rc_ = 0;
+  if (mode == 0) {
+    const float a = coeffs[0], bb = coeffs[1], cc = coeffs[2];
+    const int gx = static_cast<int>(std::min<int64_t>((rc + 255) / 256, std::max(1, num_sms() * 8 / S)));
+    ns_normalize_kernel<<<dim3(gx, S), 256, 0, stream>>>(U, Xa, rc, scal + 2 * S);
+    count_launch();
+    if (int e = check_launch("ns_normalize")) return e;
+    uint16_t* X = Xa;
+    uint16_t* Y = Xb;
+    uint16_t* Am = pool(0);
+    uint16_t* Bm = pool(1);
+    for (int t = 0; t < T; ++t) {
+      if ((rc_ = syrk(b, X, Am, nullptr))) return rc_;
+      Epilogue eb;
+      memset(&eb, 0, sizeof(eb));
+      eb.kind = 2; eb.beta = bb; eb.gamma = cc; eb.C = Am; eb.ldc = b.m; eb.strideC = b.mm; eb.D = Bm;
+      if ((rc_ = prod(b, Am, Am, eb, 1))) return rc_;
+      Epilogue ex;
+      memset(&ex, 0, sizeof(ex));
+      const bool last = t == T - 1;
+      uint16_t* dst = last ? out : Y;
+      ex.kind = 3; ex.alpha = a; ex.C = X; ex.ldc = b.c; ex.strideC = rc; ex.D = dst;
+      ex.rowsq = last ? rowsq : nullptr;
+      if ((rc_ = apply_left(b, Bm, X, ex))) return rc_;
+      std::swap(X, Y);
+    }
+    return 0;
+  }
+
+  // ---------------------------------------------------------- Gram mode --
+  auto is_reset = [&](int t) {
+    for (int i = 0; i < nresets; ++i) if (resets[i] == t) return t > 0;
+    return false;
+  };
+  bool used[kPool] = {false, false, false, false, false, false};
+  auto alloc = [&]() {
+    for (int i = 0; i < kPool; ++i) if (!used[i]) { used[i] = true; return i; }
+    return -1;
+  };
+  auto release = [&](int i) { if (i >= 0) used[i] = false; };
+
+  int R = alloc();
+  if ((rc_ = syrk(b, U, pool(R), scal + S))) return rc_;
+  const uint16_t* Xcur = U;
+  const float* pend = scal;   // the front output is scaled lazily by s
+  int Q = -1;
+  for (int t = 0; t < T; ++t) {
+    const float a = coeffs[3 * t], bb = coeffs[3 * t + 1], cc = coeffs[3 * t + 2];
+    if (is_reset(t)) {
+      uint16_t* Xn = (Xcur == Xa) ? Xb : Xa;
+      if ((rc_ = apply_left(b, pool(Q), Xcur, epi0(Xn, 0, 0, 1.0f, pend)))) return rc_;
+      release(Q); Q = -1;
+      release(R); R = alloc();
+      if ((rc_ = syrk(b, Xn, pool(R), nullptr))) return rc_;
+      Xcur = Xn;
+      pend = nullptr;
+    }
+    const int P = alloc();
+    Epilogue ep;
+    memset(&ep, 0, sizeof(ep));
+    ep.kind = 1; ep.alpha = a; ep.beta = bb; ep.gamma = cc;
+    ep.C = pool(R); ep.ldc = b.m; ep.strideC = b.mm; ep.D = pool(P);
+    if ((rc_ = prod(b, pool(R), pool(R), ep, 1))) return rc_;
+    bool p_owned_by_q = false;
+    if (Q < 0) {
+      Q = P; p_owned_by_q = true;
+    } else {
+      const int Qn = alloc();
+      if ((rc_ = prod(b, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr), 0))) return rc_;
+      release(Q); Q = Qn;
+    }
+    const bool need_r = (t < T - 1) && !is_reset(t + 1);
+    if (need_r) {
+      const int T1 = alloc();
+      if ((rc_ = prod(b, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr), 0))) return rc_;
+      const int Rn = alloc();
+      if ((rc_ = prod(b, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr), 1))) return rc_;
+      release(T1); release(R); R = Rn;
+    }
+    if (!p_owned_by_q) release(P);
+    if (R < 0 || Q < 0) { set_error("orthogonalize: workspace pool exhausted"); return -1; }
+  }
+  Epilogue ef = epi0(out, 0, 0, 1.0f, pend);
+  ef.rowsq = rowsq;
+  return apply_left(b, pool(Q), Xcur, ef);
+}
+
+}  // namespace b2o

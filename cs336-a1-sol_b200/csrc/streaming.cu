@@ -1,0 +1,650 @@
+// HBM-bound streaming kernels of the optimizer step (sm_100a):
+//   * fused AdamW (+ EMA)                 torch.optim.AdamW(fused=True), sol_modules.py:468-476
+//   * stand-alone EMA and EMA->param copy EmaWeights.update/averaged, sol_modules.py:1255-1280
+//   * NorMuon front (momentum, Nesterov)  sol_modules.py:390-394
+//   * NorMuon finish + apply              sol_modules.py:396-424
+// All kernels move 16-byte vectors, size their grids in multiples of the SM
+// count and take tensor lists by value as kernel parameters (no host->device
+// copies of pointer tables).
+#include "b2o_common.cuh"
+#include "b2o_internal.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <vector>
+
+namespace b2o {
+
+// ------------------------------------------------------------ vector I/O ---
+struct alignas(16) U16x8 { uint16_t v[8]; };
+struct alignas(16) F32x4 { float v[4]; };
+
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  __device__ static void load8(const float* p, float* o) {
+    F32x4 a = *reinterpret_cast<const F32x4*>(p);
+    F32x4 b = *reinterpret_cast<const F32x4*>(p + 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { o[i] = a.v[i]; o[4 + i] = b.v[i]; }
+  }
+  __device__ static void store8(float* p, const float* x) {
+    F32x4 a, b;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { a.v[i] = x[i]; b.v[i] = x[4 + i]; }
+    *reinterpret_cast<F32x4*>(p) = a;
+    *reinterpret_cast<F32x4*>(p + 4) = b;
+  }
+  __device__ static float load1(const float* p) { return *p; }
+  __device__ static void store1(float* p, float x) { *p = x; }
+  // value after rounding to the storage type
+  __device__ static float rnd(float x) { return x; }
+};
+template <> struct Elem<uint16_t> {  // bf16 stored as raw bits
+  __device__ static void load8(const uint16_t* p, float* o) {
+    U16x8 a = *reinterpret_cast<const U16x8*>(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = bf16_to_f32(a.v[i]);
+  }
+  __device__ static void store8(uint16_t* p, const float* x) {
+    U16x8 a;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a.v[i] = f32_to_bf16(x[i]);
+    *reinterpret_cast<U16x8*>(p) = a;
+  }
+  __device__ static float load1(const uint16_t* p) { return bf16_to_f32(*p); }
+  __device__ static void store1(uint16_t* p, float x) { *p = f32_to_bf16(x); }
+  __device__ static float rnd(float x) { return round_bf16(x); }
+};
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ================================================================ AdamW ===
+constexpr int kAdamMaxTensors = 96;
+constexpr int kAdamMaxGroups = 8;
+constexpr int kAdamThreads = 256;
+constexpr int kAdamChunk = kAdamThreads * 8 * 4;  // elements per block iteration
+
+struct AdamTable {
+  b2o_adamw_tensor t[kAdamMaxTensors];
+  b2o_adamw_group g[kAdamMaxGroups];
+  int chunk_start[kAdamMaxTensors + 1];  // prefix sum of chunks per tensor
+  int vec_ok[kAdamMaxTensors];           // 1 when every pointer is 16-byte aligned
+  int ntensors;
+  float ema_weight;
+};
+
+// One element of torch's fused AdamW (ATen/native/cuda/fused_adam_utils.cuh,
+// adam_math with ADAMW mode), extended by the cautious mask and the bf16
+// remainder of NorMuonGNS (sol_modules.py:406-424).
+struct AdamCoef {
+  float lr, b1, b2, eps, lr_wd, step_size, bc2_sqrt;
+  int wd_on, cautious;
+};
+
+__device__ __forceinline__ AdamCoef make_coef(const b2o_adamw_group& g) {
+  AdamCoef c;
+  c.lr = g.lr; c.b1 = g.beta1; c.b2 = g.beta2; c.eps = g.eps; c.lr_wd = g.lr_wd;
+  const float bc1 = 1.0f - powf(g.beta1, g.step);
+  const float bc2 = 1.0f - powf(g.beta2, g.step);
+  c.bc2_sqrt = sqrtf(bc2);
+  c.step_size = g.lr / bc1;
+  c.wd_on = g.weight_decay != 0.0f;
+  c.cautious = g.cautious;
+  return c;
+}
+
+__device__ __forceinline__ void adam_elem(const AdamCoef& c, float& w, float grad, float& m, float& v) {
+  m = fmaf(c.b1, m, fmaf(-c.b1, grad, grad));
+  const float g2 = grad * grad;
+  v = fmaf(c.b2, v, fmaf(-c.b2, g2, g2));
+  if (c.wd_on) {
+    if (c.cautious) {
+      // the update subtracted is step_size*m/denom with positive factors, so
+      // its sign is the sign of m (sol_modules.py:414-418)
+      const float mask = (m * w) > 0.0f ? 1.0f : 0.0f;
+      w = w * (1.0f - c.lr_wd * mask);
+    } else {
+      w = w - c.lr_wd * w;
+    }
+  }
+  const float denom = sqrtf(v) / c.bc2_sqrt + c.eps;
+  w = w - (c.step_size * m) / denom;
+}
+
+template <typename PT, typename ST>
+__global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_constant__ AdamTable tab) {
+  const int total_chunks = tab.chunk_start[tab.ntensors];
+  for (int chunk = blockIdx.x; chunk < total_chunks; chunk += gridDim.x) {
+    // locate the tensor owning this chunk (<= kAdamMaxTensors entries)
+    int lo = 0, hi = tab.ntensors - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tab.chunk_start[mid] <= chunk) lo = mid; else hi = mid - 1;
+    }
+    const b2o_adamw_tensor& T = tab.t[lo];
+    const AdamCoef c = make_coef(tab.g[T.group]);
+    const int64_t base = static_cast<int64_t>(chunk - tab.chunk_start[lo]) * kAdamChunk;
+    const int64_t end = min(T.numel, base + kAdamChunk);
+    PT* __restrict__ P = reinterpret_cast<PT*>(T.param);
+    const PT* __restrict__ G = reinterpret_cast<const PT*>(T.grad);
+    ST* __restrict__ M = reinterpret_cast<ST*>(T.exp_avg);
+    ST* __restrict__ V = reinterpret_cast<ST*>(T.exp_avg_sq);
+    uint16_t* __restrict__ R = T.rem;
+    float* __restrict__ E = T.ema;
+    const float ew = tab.ema_weight;
+    if (tab.vec_ok[lo]) {
+      for (int64_t i = base + static_cast<int64_t>(threadIdx.x) * 8; i + 8 <= end; i += kAdamThreads * 8) {
+        float w[8], g[8], m[8], v[8];
+        Elem<PT>::load8(P + i, w);
+        Elem<PT>::load8(G + i, g);
+        Elem<ST>::load8(M + i, m);
+        Elem<ST>::load8(V + i, v);
+        if (R) {
+          float r[8];
+          Elem<uint16_t>::load8(R + i, r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = w[k] + r[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) adam_elem(c, w[k], g[k], m[k], v[k]);
+        float pn[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pn[k] = Elem<PT>::rnd(w[k]);
+        Elem<PT>::store8(P + i, pn);
+        if (R) {
+          float r[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) r[k] = w[k] - pn[k];
+          Elem<uint16_t>::store8(R + i, r);
+        }
+        Elem<ST>::store8(M + i, m);
+        Elem<ST>::store8(V + i, v);
+        if (E) {
+          float e[8];
+          Elem<float>::load8(E + i, e);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) e[k] = torch_lerp(e[k], pn[k], ew);
+          Elem<float>::store8(E + i, e);
+        }
+      }
+      // ragged tail of the tensor (fewer than 8 elements)
+      const int64_t tail = base + ((end - base) / 8) * 8;
+      for (int64_t i = tail + threadIdx.x; i < end; i += kAdamThreads) {
+        float w = Elem<PT>::load1(P + i), g = Elem<PT>::load1(G + i);
+        float m = Elem<ST>::load1(M + i), v = Elem<ST>::load1(V + i);
+        if (R) w = w + bf16_to_f32(R[i]);
+        adam_elem(c, w, g, m, v);
+        const float pn = Elem<PT>::rnd(w);
+        Elem<PT>::store1(P + i, pn);
+        if (R) R[i] = f32_to_bf16(w - pn);
+        Elem<ST>::store1(M + i, m);
+        Elem<ST>::store1(V + i, v);
+        if (E) E[i] = torch_lerp(E[i], pn, ew);
+      }
+    } else {
+      for (int64_t i = base + threadIdx.x; i < end; i += kAdamThreads) {
+        float w = Elem<PT>::load1(P + i), g = Elem<PT>::load1(G + i);
+        float m = Elem<ST>::load1(M + i), v = Elem<ST>::load1(V + i);
+        if (R) w = w + bf16_to_f32(R[i]);
+        adam_elem(c, w, g, m, v);
+        const float pn = Elem<PT>::rnd(w);
+        Elem<PT>::store1(P + i, pn);
+        if (R) R[i] = f32_to_bf16(w - pn);
+        Elem<ST>::store1(M + i, m);
+        Elem<ST>::store1(V + i, v);
+        if (E) E[i] = torch_lerp(E[i], pn, ew);
+      }
+    }
+  }
+}
+
+int adamw_step(const b2o_adamw_tensor* tensors, int ntensors, const b2o_adamw_group* groups,
+               int ngroups, int param_dtype, int state_dtype, float ema_weight, cudaStream_t stream) {
+  if (ntensors < 0 || (ntensors > 0 && !tensors)) { set_error("adamw: bad tensor list"); return -1; }
+  if (ngroups <= 0 || ngroups > kAdamMaxGroups || !groups) { set_error("adamw: 1..8 groups required"); return -1; }
+  if (param_dtype != B2O_F32 && param_dtype != B2O_BF16) { set_error("adamw: bad param dtype"); return -1; }
+  if (state_dtype != B2O_F32 && state_dtype != B2O_BF16) { set_error("adamw: bad state dtype"); return -1; }
+  if (param_dtype == B2O_F32 && state_dtype != B2O_F32) { set_error("adamw: fp32 params need fp32 state"); return -1; }
+  for (int i = 0; i < ntensors; ++i) {
+    const b2o_adamw_tensor& t = tensors[i];
+    if (t.numel < 0 || (t.numel > 0 && (!t.param || !t.grad || !t.exp_avg || !t.exp_avg_sq))) {
+      set_error("adamw: tensor " + std::to_string(i) + " has a null pointer"); return -1;
+    }
+    if (t.group < 0 || t.group >= ngroups) { set_error("adamw: tensor group out of range"); return -1; }
+    if (t.rem && param_dtype != B2O_BF16) { set_error("adamw: remainder needs bf16 params"); return -1; }
+  }
+  int done = 0;
+  while (done < ntensors) {
+    AdamTable tab;
+    memset(&tab, 0, sizeof(tab));
+    int n = 0, chunks = 0;
+    while (done + n < ntensors && n < kAdamMaxTensors) {
+      const b2o_adamw_tensor& t = tensors[done + n];
+      const int64_t ch = (t.numel + kAdamChunk - 1) / kAdamChunk;
+      if (static_cast<int64_t>(chunks) + ch > (1ll << 30)) break;
+      tab.t[n] = t;
+      tab.chunk_start[n] = chunks;
+      tab.vec_ok[n] = aligned16(t.param) && aligned16(t.grad) && aligned16(t.exp_avg) &&
+                      aligned16(t.exp_avg_sq) && (!t.rem || aligned16(t.rem)) &&
+                      (!t.ema || aligned16(t.ema));
+      chunks += static_cast<int>(ch);
+      ++n;
+    }
+    if (n == 0) { set_error("adamw: tensor too large"); return -1; }
+    tab.chunk_start[n] = chunks;
+    tab.ntensors = n;
+    for (int g = 0; g < ngroups; ++g) tab.g[g] = groups[g];
+    tab.ema_weight = ema_weight;
+    if (chunks > 0) {
+      const int grid = std::min(chunks, num_sms() * 8);
+      if (param_dtype == B2O_F32)
+        adamw_kernel<float, float><<<grid, kAdamThreads, 0, stream>>>(tab);
+      else if (state_dtype == B2O_F32)
+        adamw_kernel<uint16_t, float><<<grid, kAdamThreads, 0, stream>>>(tab);
+      else
+        adamw_kernel<uint16_t, uint16_t><<<grid, kAdamThreads, 0, stream>>>(tab);
+      count_launch();
+      if (int e = check_launch("adamw")) return e;
+    }
+    done += n;
+  }
+  return 0;
+}
+
+// ================================================================== EMA ===
+constexpr int kEmaMax = 128;
+struct EmaTable {
+  float* s[kEmaMax];
+  const void* p[kEmaMax];
+  int64_t n[kEmaMax];
+  int chunk_start[kEmaMax + 1];
+  int vec_ok[kEmaMax];
+  int count;
+  float w;
+};
+constexpr int kEmaChunk = 256 * 8 * 4;
+
+template <typename PT, bool TO_PARAM>
+__global__ void __launch_bounds__(256) ema_kernel(const __grid_constant__ EmaTable tab) {
+  const int total = tab.chunk_start[tab.count];
+  for (int chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    int lo = 0, hi = tab.count - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tab.chunk_start[mid] <= chunk) lo = mid; else hi = mid - 1;
+    }
+    float* S = tab.s[lo];
+    PT* P = reinterpret_cast<PT*>(const_cast<void*>(tab.p[lo]));
+    const int64_t base = static_cast<int64_t>(chunk - tab.chunk_start[lo]) * kEmaChunk;
+    const int64_t end = min(tab.n[lo], base + kEmaChunk);
+    int64_t scalar_from = base;
+    if (tab.vec_ok[lo]) {
+      for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += 256 * 8) {
+        float s[8], p[8];
+        Elem<float>::load8(S + i, s);
+        if (TO_PARAM) {
+          Elem<PT>::store8(P + i, s);
+        } else {
+          Elem<PT>::load8(P + i, p);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) s[k] = torch_lerp(s[k], p[k], tab.w);
+          Elem<float>::store8(S + i, s);
+        }
+      }
+      scalar_from = base + ((end - base) / 8) * 8;
+    }
+    for (int64_t i = scalar_from + threadIdx.x; i < end; i += 256) {
+      if (TO_PARAM) Elem<PT>::store1(P + i, S[i]);
+      else S[i] = torch_lerp(S[i], Elem<PT>::load1(P + i), tab.w);
+    }
+  }
+}
+
+template <bool TO_PARAM>
+static int ema_launch(float* const* shadows, const void* const* params, const int64_t* numels, int nt,
+                      int param_dtype, float w, cudaStream_t stream) {
+  if (nt < 0 || (nt > 0 && (!shadows || !params || !numels))) { set_error("ema: bad lists"); return -1; }
+  if (param_dtype != B2O_F32 && param_dtype != B2O_BF16) { set_error("ema: bad dtype"); return -1; }
+  int done = 0;
+  while (done < nt) {
+    EmaTable tab;
+    memset(&tab, 0, sizeof(tab));
+    int n = 0, chunks = 0;
+    while (done + n < nt && n < kEmaMax) {
+      const int i = done + n;
+      if (numels[i] > 0 && (!shadows[i] || !params[i])) { set_error("ema: null pointer"); return -1; }
+      tab.s[n] = shadows[i];
+      tab.p[n] = params[i];
+      tab.n[n] = numels[i];
+      tab.chunk_start[n] = chunks;
+      tab.vec_ok[n] = aligned16(shadows[i]) && aligned16(params[i]);
+      chunks += static_cast<int>((numels[i] + kEmaChunk - 1) / kEmaChunk);
+      ++n;
+    }
+    tab.chunk_start[n] = chunks;
+    tab.count = n;
+    tab.w = w;
+    if (chunks > 0) {
+      const int grid = std::min(chunks, num_sms() * 8);
+      if (param_dtype == B2O_F32) ema_kernel<float, TO_PARAM><<<grid, 256, 0, stream>>>(tab);
+      else ema_kernel<uint16_t, TO_PARAM><<<grid, 256, 0, stream>>>(tab);
+      count_launch();
+      if (int e = check_launch("ema")) return e;
+    }
+    done += n;
+  }
+  return 0;
+}
+
+int ema_update(float* const* shadows, const void* const* params, const int64_t* numels, int nt,
+               int param_dtype, float w, cudaStream_t stream) {
+  return ema_launch<false>(shadows, params, numels, nt, param_dtype, w, stream);
+}
+int ema_copy_to_params(const float* const* shadows, void* const* params, const int64_t* numels, int nt,
+                       int param_dtype, cudaStream_t stream) {
+  return ema_launch<true>(const_cast<float* const*>(shadows), const_cast<const void* const*>(params),
+                          numels, nt, param_dtype, 0.0f, stream);
+}
+
+// ======================================================= NorMuon front ===
+constexpr int kMaxBatch = 64;          // matrices per NorMuon launch
+constexpr int kFrontThreads = 256;
+constexpr int kFrontPart = kFrontThreads * 8 * 8;  // elements per partial sum
+
+struct FrontTable {
+  const void* g[kMaxBatch];
+  void* buf[kMaxBatch];
+};
+
+int normuon_front_parts(int64_t rc) { return static_cast<int>((rc + kFrontPart - 1) / kFrontPart); }
+
+template <typename T>
+__global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(
+    const __grid_constant__ FrontTable tab, int64_t rc, int nparts, float w_small, float w_large,
+    int nesterov, int vec_ok, uint16_t* __restrict__ U, float* __restrict__ partial) {
+  const int s = blockIdx.y;
+  const T* G = reinterpret_cast<const T*>(tab.g[s]);
+  T* B = reinterpret_cast<T*>(tab.buf[s]);
+  uint16_t* Us = U + static_cast<int64_t>(s) * rc;
+  float acc = 0.f;
+  for (int part = blockIdx.x; part < nparts; part += gridDim.x) {
+    const int64_t base = static_cast<int64_t>(part) * kFrontPart;
+    const int64_t end = min(rc, base + kFrontPart);
+    float pacc = 0.f;
+    int64_t scalar_from = base;
+    if (vec_ok) {
+      for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += kFrontThreads * 8) {
+        float g[8], b[8], u[8];
+        Elem<T>::load8(G + i, g);
+        Elem<T>::load8(B + i, b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          b[k] = Elem<T>::rnd(torch_lerp(b[k], g[k], w_small));   // buf.lerp_(g, 1-beta)
+          u[k] = nesterov ? Elem<T>::rnd(torch_lerp(g[k], b[k], w_large)) : b[k];  // g.lerp(buf, beta)
+          u[k] = round_bf16(u[k]);                                 // X = u.bfloat16()
+          pacc = fmaf(u[k], u[k], pacc);
+        }
+        Elem<T>::store8(B + i, b);
+        Elem<uint16_t>::store8(Us + i, u);
+      }
+      scalar_from = base + ((end - base) / 8) * 8;
+    }
+    for (int64_t i = scalar_from + threadIdx.x; i < end; i += kFrontThreads) {
+      const float g = Elem<T>::load1(G + i);
+      float b = Elem<T>::load1(B + i);
+      b = Elem<T>::rnd(torch_lerp(b, g, w_small));
+      float u = nesterov ? Elem<T>::rnd(torch_lerp(g, b, w_large)) : b;
+      u = round_bf16(u);
+      pacc = fmaf(u, u, pacc);
+      Elem<T>::store1(B + i, b);
+      Us[i] = f32_to_bf16(u);
+    }
+    // deterministic block reduction of this part
+    __shared__ float red[kFrontThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) pacc += __shfl_xor_sync(0xffffffffu, pacc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = pacc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int k = 0; k < kFrontThreads / 32; ++k) t += red[k];
+      partial[static_cast<int64_t>(s) * nparts + part] = t;
+    }
+    __syncthreads();
+  }
+  (void)acc;
+}
+
+int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int c, int dtype,
+                  float w_small, float w_large, int nesterov, uint16_t* U, float* partial,
+                  cudaStream_t stream) {
+  if (S <= 0 || S > kMaxBatch) { set_error("normuon_front: 1..64 matrices per batch"); return -1; }
+  if (r <= 0 || c <= 0 || !grads || !bufs || !U || !partial) { set_error("normuon_front: bad args"); return -1; }
+  if (dtype != B2O_F32 && dtype != B2O_BF16) { set_error("normuon_front: bad dtype"); return -1; }
+  FrontTable tab;
+  memset(&tab, 0, sizeof(tab));
+  int vec_ok = aligned16(U);
+  const int64_t rc = static_cast<int64_t>(r) * c;
+  if ((rc * 2) % 16) vec_ok = 0;
+  for (int s = 0; s < S; ++s) {
+    if (!grads[s] || !bufs[s]) { set_error("normuon_front: null matrix pointer"); return -1; }
+    tab.g[s] = grads[s];
+    tab.buf[s] = bufs[s];
+    vec_ok = vec_ok && aligned16(grads[s]) && aligned16(bufs[s]);
+  }
+  const int nparts = normuon_front_parts(rc);
+  dim3 grid(nparts, S);
+  if (dtype == B2O_F32)
+    normuon_front_kernel<float><<<grid, kFrontThreads, 0, stream>>>(tab, rc, nparts, w_small, w_large,
+                                                                     nesterov, vec_ok, U, partial);
+  else
+    normuon_front_kernel<uint16_t><<<grid, kFrontThreads, 0, stream>>>(tab, rc, nparts, w_small, w_large,
+                                                                        nesterov, vec_ok, U, partial);
+  count_launch();
+  return check_launch("normuon_front");
+}
+
+// ====================================================== NorMuon finish ===
+// One CTA per matrix. Reduces the GEMM's per-tile row partials of o^2 into
+// row sums, updates v_row (sol_modules.py:398) and produces the per-row factor
+// 1/(sqrt(v_row)+1e-10) (:399) and the per-matrix norm-restoring factor
+// vnorm/(||o*inv||+1e-10) (:397, :400).
+struct VrowTable { float* v[kMaxBatch]; };
+
+__device__ float block_sum_1024(float x, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+    red[32] = t;
+  }
+  __syncthreads();
+  t = red[32];
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(1024) normuon_finish_kernel(
+    const __grid_constant__ VrowTable vt, const float* __restrict__ rowsq, int r, int c, int ntn,
+    float w_beta2, float* __restrict__ scratch) {
+  __shared__ float red[33];
+  const int s = blockIdx.x;
+  float* inv = scratch + static_cast<int64_t>(s) * (r + 4);
+  const float* part = rowsq + static_cast<int64_t>(s) * ntn * r;
+  float* vrow = vt.v[s];
+  float sumsq = 0.f, n1 = 0.f;
+  for (int i = threadIdx.x; i < r; i += blockDim.x) {
+    float rs = 0.f;
+    for (int t = 0; t < ntn; ++t) rs += part[static_cast<int64_t>(t) * r + i];
+    sumsq += rs;
+    const float mean = rs / static_cast<float>(c);
+    const float v = torch_lerp(vrow[i], mean, w_beta2);
+    vrow[i] = v;
+    const float iv = __frcp_rn(sqrtf(v) + 1e-10f);
+    inv[i] = iv;
+    n1 = fmaf(rs * iv, iv, n1);
+  }
+  const float tot = block_sum_1024(sumsq, red);
+  const float tot1 = block_sum_1024(n1, red);
+  if (threadIdx.x == 0) inv[r] = sqrtf(tot) / (sqrtf(tot1) + 1e-10f);
+}
+
+// ======================================================= NorMuon apply ===
+struct ApplyTable {
+  void* p[kMaxBatch];
+  uint16_t* rem[kMaxBatch];
+  float* ema[kMaxBatch];
+};
+
+struct ApplyArgs {
+  int64_t rc;
+  int r, c, nparts, has_rem, has_ema, wd_on, cautious, vec_ok;
+  float neg_lr, lr_wd, wd_factor, shape_scale, ema_w;
+};
+
+// mode: 0 = fp32 params; 1 = bf16 params with remainder (bf16_master);
+//       2 = bf16 params without remainder (every op rounds to bf16 as torch does).
+template <int MODE>
+__device__ __forceinline__ void apply_elem(const ApplyArgs& a, float o3, float& w, float& rem_out) {
+  if (MODE == 2) {
+    // w is the bf16 param; torch evaluates each op in fp32 and rounds to bf16
+    if (a.wd_on) {
+      // mask = (o * w) > 0 in fp32; factor = bf16(1 - bf16(lr*wd*mask)) (sol_modules.py:417)
+      // without the cautious mask the factor is the Python double 1 - lr*wd (:420)
+      const float f = a.cautious ? round_bf16(1.0f - round_bf16(a.lr_wd * ((o3 * w) > 0.f ? 1.f : 0.f)))
+                                 : a.wd_factor;
+      w = round_bf16(w * f);
+    }
+    w = round_bf16(fmaf(a.neg_lr, round_bf16(o3), w));
+  } else {
+    if (a.wd_on) {
+      const float f = a.cautious ? (1.0f - a.lr_wd * ((o3 * w) > 0.f ? 1.f : 0.f)) : a.wd_factor;
+      w = w * f;
+    }
+    w = fmaf(a.neg_lr, o3, w);
+    if (MODE == 1) {
+      const float pn = round_bf16(w);
+      rem_out = w - pn;   // exact in fp32; rounded to bf16 on store
+      w = pn;
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256) normuon_apply_kernel(
+    const __grid_constant__ ApplyTable tab, const __grid_constant__ ApplyArgs a,
+    const uint16_t* __restrict__ O, const float* __restrict__ scratch) {
+  const int s = blockIdx.y;
+  const float* inv = scratch + static_cast<int64_t>(s) * (a.r + 4);
+  const float f = inv[a.r];
+  const uint16_t* Os = O + static_cast<int64_t>(s) * a.rc;
+  float* E = a.has_ema ? tab.ema[s] : nullptr;
+  uint16_t* R = a.has_rem ? tab.rem[s] : nullptr;
+  using PT = typename std::conditional<MODE == 0, float, uint16_t>::type;
+  PT* P = reinterpret_cast<PT*>(tab.p[s]);
+  const int64_t per_part = 256 * 8 * 4;
+  for (int part = blockIdx.x; part * per_part < a.rc; part += gridDim.x) {
+    const int64_t base = static_cast<int64_t>(part) * per_part;
+    const int64_t end = min(a.rc, base + per_part);
+    int64_t scalar_from = base;
+    if (a.vec_ok) {
+      for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += 256 * 8) {
+        float o[8], w[8], rm[8];
+        Elem<uint16_t>::load8(Os + i, o);
+        Elem<PT>::load8(P + i, w);
+        if (MODE == 1) {
+          float r0[8];
+          Elem<uint16_t>::load8(R + i, r0);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = w[k] + r0[k];
+        }
+        // 8 consecutive elements may straddle a row boundary when c % 8 != 0
+        // (excluded by vec_ok), so one row index serves all 8.
+        const int row = static_cast<int>(i / a.c);
+        const float iv = inv[row];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float o3 = ((o[k] * iv) * f) * a.shape_scale;
+          apply_elem<MODE>(a, o3, w[k], rm[k]);
+        }
+        Elem<PT>::store8(P + i, w);
+        if (MODE == 1) Elem<uint16_t>::store8(R + i, rm);
+        if (E) {
+          float e[8];
+          Elem<float>::load8(E + i, e);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) e[k] = torch_lerp(e[k], w[k], a.ema_w);
+          Elem<float>::store8(E + i, e);
+        }
+      }
+      scalar_from = base + ((end - base) / 8) * 8;
+    }
+    for (int64_t i = scalar_from + threadIdx.x; i < end; i += 256) {
+      float w = Elem<PT>::load1(P + i), rm = 0.f;
+      if (MODE == 1) w = w + bf16_to_f32(R[i]);
+      const int row = static_cast<int>(i / a.c);
+      const float o3 = ((bf16_to_f32(Os[i]) * inv[row]) * f) * a.shape_scale;
+      apply_elem<MODE>(a, o3, w, rm);
+      Elem<PT>::store1(P + i, w);
+      if (MODE == 1) R[i] = f32_to_bf16(rm);
+      if (E) E[i] = torch_lerp(E[i], w, a.ema_w);
+    }
+  }
+}
+
+int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
+                  uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
+                  float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
+                  float w_beta2, float ema_weight, float* scratch, cudaStream_t stream) {
+  if (S <= 0 || S > kMaxBatch) { set_error("normuon_apply: 1..64 matrices per batch"); return -1; }
+  if (r <= 0 || c <= 0 || !O || !rowsq || !params || !vrows || !scratch) {
+    set_error("normuon_apply: bad args"); return -1;
+  }
+  if (param_dtype != B2O_F32 && param_dtype != B2O_BF16) { set_error("normuon_apply: bad dtype"); return -1; }
+  if (rems && param_dtype != B2O_BF16) { set_error("normuon_apply: remainder needs bf16 params"); return -1; }
+  VrowTable vt;
+  memset(&vt, 0, sizeof(vt));
+  ApplyTable tab;
+  memset(&tab, 0, sizeof(tab));
+  ApplyArgs a;
+  memset(&a, 0, sizeof(a));
+  a.rc = static_cast<int64_t>(r) * c;
+  a.r = r; a.c = c;
+  a.has_rem = rems != nullptr;
+  a.has_ema = emas != nullptr;
+  a.wd_on = wd_on; a.cautious = cautious;
+  a.neg_lr = neg_lr; a.lr_wd = lr_wd; a.wd_factor = wd_factor; a.shape_scale = shape_scale; a.ema_w = ema_weight;
+  int vec_ok = (c % 8 == 0) && aligned16(O);
+  for (int s = 0; s < S; ++s) {
+    if (!params[s] || !vrows[s] || (rems && !rems[s]) || (emas && !emas[s])) {
+      set_error("normuon_apply: null matrix pointer"); return -1;
+    }
+    tab.p[s] = params[s];
+    tab.rem[s] = rems ? rems[s] : nullptr;
+    tab.ema[s] = emas ? emas[s] : nullptr;
+    vt.v[s] = vrows[s];
+    vec_ok = vec_ok && aligned16(params[s]) && (!rems || aligned16(rems[s])) && (!emas || aligned16(emas[s]));
+  }
+  a.vec_ok = vec_ok;
+  const int ntn = (c + 255) / 256;
+  normuon_finish_kernel<<<S, 1024, 0, stream>>>(vt, rowsq, r, c, ntn, w_beta2, scratch);
+  count_launch();
+  if (int e = check_launch("normuon_finish")) return e;
+  const int64_t per_part = 256 * 8 * 4;
+  const int parts = static_cast<int>((a.rc + per_part - 1) / per_part);
+  const int gx = std::max(1, std::min(parts, (num_sms() * 8 + S - 1) / S));
+  dim3 grid(gx, S);
+  if (param_dtype == B2O_F32)
+    normuon_apply_kernel<0><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+  else if (rems)
+    normuon_apply_kernel<1><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+  else
+    normuon_apply_kernel<2><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+  count_launch();
+  return check_launch("normuon_apply");
+}
+
+}  // namespace b2o

@@ -1,0 +1,149 @@
+"""ctypes binding of libb2o.so (the C ABI declared in include/b2o.h).
+
+The engine has no CPU fallback: every compute entry point here raises when the
+shared library is missing or when no CUDA device is present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libb2o.so"
+
+F32 = 0
+BF16 = 1
+
+c_void_p = C.c_void_p
+c_int = C.c_int
+c_int64 = C.c_int64
+c_float = C.c_float
+
+
+class AdamwTensor(C.Structure):
+    _fields_ = [
+        ("param", c_void_p),
+        ("rem", c_void_p),
+        ("grad", c_void_p),
+        ("exp_avg", c_void_p),
+        ("exp_avg_sq", c_void_p),
+        ("ema", c_void_p),
+        ("numel", c_int64),
+        ("group", C.c_int32),
+        ("_pad", C.c_int32),
+    ]
+
+
+class AdamwGroup(C.Structure):
+    _fields_ = [
+        ("lr", c_float),
+        ("beta1", c_float),
+        ("beta2", c_float),
+        ("eps", c_float),
+        ("weight_decay", c_float),
+        ("lr_wd", c_float),
+        ("step", c_float),
+        ("cautious", C.c_int32),
+    ]
+
+
+# name -> (restype, argtypes); mirrors include/b2o.h one to one
+SIGNATURES = {
+    "b2o_version": (c_int, []),
+    "b2o_last_error": (c_int, [C.c_char_p, c_int]),
+    "b2o_launch_count": (c_int64, []),
+    "b2o_check_device_error": (c_int, [c_void_p]),
+    "b2o_num_sms": (c_int, []),
+    "b2o_adamw_step": (c_int, [C.POINTER(AdamwTensor), c_int, C.POINTER(AdamwGroup), c_int, c_int, c_int,
+                               c_float, c_void_p]),
+    "b2o_ema_update": (c_int, [C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_int64), c_int, c_int,
+                               c_float, c_void_p]),
+    "b2o_ema_copy_to_params": (c_int, [C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_int64), c_int,
+                                       c_int, c_void_p]),
+    "b2o_normuon_front_parts": (c_int, [c_int64]),
+    "b2o_normuon_front": (c_int, [C.POINTER(c_void_p), C.POINTER(c_void_p), c_int, c_int, c_int, c_int, c_float,
+                                  c_float, c_int, c_void_p, c_void_p, c_void_p]),
+    "b2o_ortho_workspace_bytes": (c_int64, [c_int, c_int, c_int]),
+    "b2o_orthogonalize": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, C.POINTER(c_float), c_int,
+                                  C.POINTER(c_int), c_int, c_float, c_float, c_void_p, c_int64, c_void_p,
+                                  c_void_p, c_void_p]),
+    "b2o_normuon_apply_scratch_floats": (c_int64, [c_int, c_int]),
+    "b2o_normuon_apply": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, C.POINTER(c_void_p),
+                                  C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_void_p), c_int, c_float,
+                                  c_float, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p]),
+    "b2o_gemm_bf16": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int, c_void_p,
+                              c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
+                              c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
+    "b2o_gemm_bf16_simt": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int,
+                                   c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
+                                   c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Loads libb2o.so (building it first if this tree has nvcc and no .so)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            from . import build as _build
+            _build.build()
+        lib = C.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = C.create_string_buffer(1024)
+    lib.b2o_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"libb2o {what} failed (status {rc}): {last_error()}")
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what}: the B200 engine runs on CUDA tensors only (got {t.device}); "
+                           "there is no CPU fallback")
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr_array(ptrs) -> C.Array:
+    return (c_void_p * len(ptrs))(*[int(x) if x else None for x in ptrs])
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.float32:
+        return F32
+    if dt == torch.bfloat16:
+        return BF16
+    raise TypeError(f"unsupported dtype {dt}; the engine handles float32 and bfloat16")
+
+
+def launch_count() -> int:
+    return int(load().b2o_launch_count())
+
+
+def device_error(stream: int | None = None) -> int:
+    """Synchronises the stream and returns/clears the device error word."""
+    lib = load()
+    return int(lib.b2o_check_device_error(stream if stream is not None else stream_ptr()))

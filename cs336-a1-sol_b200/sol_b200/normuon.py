@@ -1,0 +1,206 @@
+"""NorMuonGNS on the B200 engine.
+
+Drop-in for ``transformer_lm.sol_modules.NorMuonGNS`` (transformer_lm/sol_modules.py:330-425):
+same constructor arguments, param-group keys, per-parameter state
+(``momentum_buffer`` param dtype (r, c), ``v_row`` fp32 (r, 1), ``mant_rem`` bf16
+(r, c) when ``bf16_master`` and the param is bf16) and the overridable
+``_orthogonalize_batch(U, ns_steps)`` hook (:366).
+
+Per exact-shape batch (the reference buckets by ``tuple(p.shape)``, :380-383)
+one step is four launches sequences of libb2o, with no stacking copies:
+  front  (momentum lerp + Nesterov, :390-394)  -> u (S, r, c) bf16 + norm partials
+  orthogonalise (:395; GEMMs on tcgen05)       -> o (S, r, c) bf16 + row sums of o^2
+  finish (v_row lerp + scale factors, :396-401) and
+  apply  (cautious WD, update, bf16 mantissa split, EMA; :402-424).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from collections import OrderedDict
+
+import torch
+
+from . import _lib
+from .ema import register_optimizer
+from .polar_express import table_for
+
+MAX_BATCH = 64  # matrices per launch (kernel-parameter tables)
+
+
+class NorMuonGNS(torch.optim.Optimizer):
+    """NorMuon (Muon + per-row second moment) with a Newton-Schulz orthogonaliser.
+
+    Extra keyword arguments (not in the reference signature):
+      orthogonalizer: "gram" (Gram Newton-Schulz, the path the reference takes when
+          gram-newton-schulz is installed) or "quintic" (the reference's fallback,
+          zeropower_via_newtonschulz5, restated on the same GEMM engine).
+      coefficients: "polar_express" or "quintic" coefficient table for "gram".
+      reset_iterations: Gram restart steps (the reference passes [2], :357).
+    """
+
+    def __init__(self, params, lr=2e-3, momentum=0.95, beta2=0.95, nesterov=True, ns_steps=5,
+                 weight_decay=0.0, cautious_wd=False, bf16_master=False, *, orthogonalizer="gram",
+                 coefficients="polar_express", reset_iterations=(2,), norm_eps=1e-7, norm_safety=None):
+        super().__init__(params, dict(lr=lr, momentum=momentum, beta2=beta2, nesterov=nesterov,
+                                      ns_steps=ns_steps, weight_decay=weight_decay))
+        if orthogonalizer not in ("gram", "quintic"):
+            raise ValueError("orthogonalizer must be 'gram' or 'quintic'")
+        self.cautious_wd = cautious_wd
+        self.bf16_master = bf16_master
+        self.orthogonalizer = orthogonalizer
+        self.coefficients = "quintic" if orthogonalizer == "quintic" else coefficients
+        self.reset_iterations = tuple(int(x) for x in reset_iterations)
+        self.norm_eps = float(norm_eps)
+        if norm_safety is None:
+            norm_safety = 1.01 if self.coefficients == "polar_express" else 1.0
+        self.norm_safety = float(norm_safety)
+        self._ws = {}
+        self._tables = {}
+        self._owned = None         # set of id(param) this rank updates (sharded step), None = all
+        self._ema = None           # EmaWeights folded into the apply pass (set when it arms)
+        self._ema_weight = 0.0
+        register_optimizer(self)
+
+    # ------------------------------------------------------------------ hooks
+    def _orthogonalize_batch(self, U, ns_steps):
+        """U: (S, r, c) bf16 CUDA tensor -> (S, r, c) bf16 (one call per shape batch)."""
+        U = U.contiguous()
+        _lib.require_cuda(U, "NorMuonGNS._orthogonalize_batch")
+        S, r, c = U.shape
+        ws = self._workspace(U.device, S, r, c)
+        parts = ws["partial"].view(S, -1)
+        parts.zero_()
+        parts[:, 0] = U.float().pow(2).sum(dim=(1, 2))
+        out = torch.empty_like(U)
+        self._ortho(U, ws["partial"], S, r, c, ns_steps, out, ws)
+        return out
+
+    # -------------------------------------------------------------- internals
+    def _table(self, ns_steps):
+        key = (self.coefficients, ns_steps)
+        if key not in self._tables:
+            rows = table_for(self.coefficients, ns_steps)
+            flat = [float(v) for row in rows for v in row]
+            coeffs = (C.c_float * len(flat))(*flat)
+            resets = (C.c_int * max(1, len(self.reset_iterations)))(*self.reset_iterations)
+            self._tables[key] = (coeffs, resets, len(self.reset_iterations))
+        return self._tables[key]
+
+    def _workspace(self, device, S, r, c):
+        key = (device, S, r, c)
+        ws = self._ws.get(key)
+        if ws is None:
+            lib = _lib.load()
+            rc = r * c
+            nparts = lib.b2o_normuon_front_parts(rc)
+            ntn = (c + 255) // 256
+            wbytes = lib.b2o_ortho_workspace_bytes(S, r, c)
+            ws = {
+                "u": torch.empty((S, r, c), dtype=torch.bfloat16, device=device),
+                "o": torch.empty((S, r, c), dtype=torch.bfloat16, device=device),
+                "partial": torch.zeros(S * nparts, dtype=torch.float32, device=device),
+                "rowsq": torch.zeros(S * ntn * r, dtype=torch.float32, device=device),
+                "scratch": torch.empty(lib.b2o_normuon_apply_scratch_floats(S, r), dtype=torch.float32,
+                                       device=device),
+                "ortho": torch.empty(wbytes, dtype=torch.uint8, device=device),
+            }
+            self._ws[key] = ws
+        return ws
+
+    def _ortho(self, U, partial, S, r, c, ns_steps, out, ws):
+        lib = _lib.load()
+        coeffs, resets, nres = self._table(ns_steps)
+        mode = 0 if self.orthogonalizer == "quintic" else 1
+        rc = lib.b2o_orthogonalize(U.data_ptr(), partial.data_ptr(), S, r, c, mode, coeffs, ns_steps, resets,
+                                   nres, self.norm_eps, self.norm_safety, ws["ortho"].data_ptr(),
+                                   ws["ortho"].numel(), out.data_ptr(), ws["rowsq"].data_ptr(),
+                                   _lib.stream_ptr(U.device))
+        _lib.check(rc, "orthogonalize")
+
+    def _hook_overridden(self):
+        return ("_orthogonalize_batch" in self.__dict__ or
+                type(self)._orthogonalize_batch is not NorMuonGNS._orthogonalize_batch)
+
+    def _init_state(self, p):
+        st = self.state[p]
+        if "momentum_buffer" not in st:
+            st["momentum_buffer"] = torch.zeros_like(p)
+            st["v_row"] = torch.zeros_like(p[..., 0:1], dtype=torch.float32)
+        if self.bf16_master and p.dtype == torch.bfloat16 and "mant_rem" not in st:
+            st["mant_rem"] = torch.zeros_like(p)
+        return st
+
+    def _step_batch(self, params, shape, group):
+        lib = _lib.load()
+        p0 = params[0]
+        _lib.require_cuda(p0, "NorMuonGNS.step")
+        dev = p0.device
+        S = len(params)
+        r, c = int(shape[-2]), int(shape[-1])
+        for p in params:
+            if p.dim() != 2:
+                raise ValueError("NorMuonGNS handles 2-D parameters only")
+            if p.grad.dtype != p.dtype or not p.is_contiguous() or not p.grad.is_contiguous():
+                raise ValueError("NorMuonGNS needs contiguous params and grads of the param dtype")
+        states = [self._init_state(p) for p in params]
+        dt = _lib.dtype_code(p0.dtype)
+        ws = self._workspace(dev, S, r, c)
+        stream = _lib.stream_ptr(dev)
+        beta, beta2 = float(group["momentum"]), float(group["beta2"])
+        lr, wd = float(group["lr"]), float(group["weight_decay"])
+        ns_steps, nesterov = int(group["ns_steps"]), bool(group["nesterov"])
+
+        grads = _lib.ptr_array([p.grad.data_ptr() for p in params])
+        bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in states])
+        rc = lib.b2o_normuon_front(grads, bufs, S, r, c, dt, 1.0 - beta, beta, int(nesterov),
+                                   ws["u"].data_ptr(), ws["partial"].data_ptr(), stream)
+        _lib.check(rc, "normuon_front")
+
+        if self._hook_overridden():
+            o = self._orthogonalize_batch(ws["u"], ns_steps)
+            o = o.to(torch.bfloat16).contiguous()
+            ntn = (c + 255) // 256
+            rs = ws["rowsq"].view(S, ntn, r)
+            rs.zero_()
+            rs[:, 0, :] = o.float().pow(2).sum(dim=-1)
+        else:
+            o = ws["o"]
+            self._ortho(ws["u"], ws["partial"], S, r, c, ns_steps, o, ws)
+
+        mt = self.bf16_master and p0.dtype == torch.bfloat16
+        pptr = _lib.ptr_array([p.data_ptr() for p in params])
+        rems = _lib.ptr_array([st["mant_rem"].data_ptr() for st in states]) if mt else None
+        vrows = _lib.ptr_array([st["v_row"].data_ptr() for st in states])
+        emas = None
+        if self._ema is not None:
+            shadows = [self._ema._lookup(p) for p in params]
+            if all(s is not None for s in shadows):
+                emas = _lib.ptr_array([s.data_ptr() for s in shadows])
+                for p in params:
+                    self._ema._mark(p)
+        wd_on = 1 if wd else 0
+        shape_scale = math.sqrt(max(1.0, r / c))
+        rc = lib.b2o_normuon_apply(o.data_ptr(), ws["rowsq"].data_ptr(), S, r, c, pptr, rems, emas, vrows, dt,
+                                   -lr, lr * wd, 1.0 - lr * wd, wd_on, int(bool(self.cautious_wd and wd)),
+                                   shape_scale, 1.0 - beta2, self._ema_weight, ws["scratch"].data_ptr(), stream)
+        _lib.check(rc, "normuon_apply")
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            by_shape = OrderedDict()  # exact-shape buckets in param order (sol_modules.py:380-383)
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                if self._owned is not None and id(p) not in self._owned:
+                    continue
+                by_shape.setdefault(tuple(p.shape), []).append(p)
+            for shape, params in by_shape.items():
+                for i in range(0, len(params), MAX_BATCH):
+                    self._step_batch(params[i:i + MAX_BATCH], shape, group)
+        return loss

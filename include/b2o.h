@@ -1,0 +1,185 @@
+/*
+ * b2o.h — C ABI of the B200 optimizer-step engine (libb2o.so).
+ *
+ * The engine replaces the optimizer step that the reference training loop runs
+ * after loss.backward() (transformer_lm/train_sol.py:500-507):
+ *   muon.step()   -> NorMuonGNS.step            transformer_lm/sol_modules.py:372-425
+ *   adamw.step()  -> torch.optim.AdamW(fused)   transformer_lm/sol_modules.py:476
+ *   ema.update()  -> EmaWeights.update          transformer_lm/sol_modules.py:1255-1268
+ *
+ * Conventions
+ *   - Every pointer argument named d_* is a device pointer owned by the caller
+ *     (PyTorch's caching allocator in the Python host layer). The library never
+ *     allocates, frees or synchronises device memory on its own, except inside
+ *     b2o_check_device_error(), which synchronises the given stream.
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and the
+ *     call returns without waiting.
+ *   - Return value: 0 = ok; negative = invalid argument detected on the host
+ *     (nothing was launched; b2o_last_error() has the message); positive = a
+ *     CUDA launch/runtime error code.
+ *   - Device-side failures (a bounded wait that ran out) set a device error word
+ *     instead of trapping; b2o_check_device_error() reads and clears it.
+ *   - dtype codes: B2O_F32 = 0, B2O_BF16 = 1.
+ */
+#ifndef B2O_H_
+#define B2O_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2O_F32 0
+#define B2O_BF16 1
+
+/* Error/status plumbing (no reference counterpart: the reference raises Python
+ * exceptions from torch; these carry the same information across the C ABI). */
+int b2o_version(void);
+int b2o_last_error(char* buf, int buflen);
+/* Number of kernels this library has launched since load (monotonic). */
+int64_t b2o_launch_count(void);
+/* Synchronises `stream`, returns the device error word (0 = none) and clears it. */
+int b2o_check_device_error(void* stream);
+/* Number of SMs of the current device (used by the host layer for grid sizing). */
+int b2o_num_sms(void);
+
+/* ------------------------------------------------------------------------ *
+ * Fused AdamW (+ optional EMA) over a list of tensors.
+ * Replaces torch.optim.AdamW(groups, betas, eps, fused=True)
+ * (transformer_lm/sol_modules.py:468-476; math torch/optim/adam.py:347-547 and
+ * the fused kernel formula in ATen/native/cuda/fused_adam_utils.cuh) and, when
+ * `ema` is non-NULL, EmaWeights.update for the same tensors
+ * (transformer_lm/sol_modules.py:1267-1268).
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  void* param;          /* param_dtype, numel elements                       */
+  uint16_t* rem;        /* bf16 bit pattern of the low-mantissa remainder or NULL */
+  const void* grad;     /* param_dtype                                        */
+  void* exp_avg;        /* state_dtype                                        */
+  void* exp_avg_sq;     /* state_dtype                                        */
+  float* ema;           /* fp32 EMA shadow or NULL                            */
+  int64_t numel;
+  int32_t group;        /* index into the group table                         */
+  int32_t _pad;
+} b2o_adamw_tensor;
+
+typedef struct {
+  float lr;
+  float beta1;
+  float beta2;
+  float eps;
+  float weight_decay;
+  float lr_wd;          /* fp32(lr * weight_decay), rounded once on the host  */
+  float step;           /* step count after increment (torch's state["step"]) */
+  int32_t cautious;     /* 1: decay only where update * w > 0                 */
+} b2o_adamw_group;
+
+/* param_dtype: B2O_F32 or B2O_BF16. state_dtype: B2O_F32 or B2O_BF16 (must equal
+ * param_dtype unless param is bf16 and state is fp32). rem must be NULL unless
+ * param_dtype is bf16. ema_weight = fp32(1 - decay); ignored where ema == NULL. */
+int b2o_adamw_step(const b2o_adamw_tensor* tensors, int ntensors,
+                   const b2o_adamw_group* groups, int ngroups,
+                   int param_dtype, int state_dtype, float ema_weight, void* stream);
+
+/* Stand-alone EMA: shadow = lerp(shadow, float(param), weight) for each tensor.
+ * Replaces EmaWeights.update/_update_slow (transformer_lm/sol_modules.py:1255-1268). */
+int b2o_ema_update(float* const* shadows, const void* const* params, const int64_t* numels,
+                   int ntensors, int param_dtype, float weight, void* stream);
+
+/* EMA swap for evaluation: param = param_dtype(shadow) for each tensor
+ * (EmaWeights.averaged, transformer_lm/sol_modules.py:1270-1280; the backup and
+ * restore are plain device copies done by the caller). */
+int b2o_ema_copy_to_params(const float* const* shadows, void* const* params,
+                           const int64_t* numels, int ntensors, int param_dtype,
+                           void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * NorMuon, one shape-batch of S matrices of shape (r, c).
+ * Replaces the per-shape body of NorMuonGNS.step (transformer_lm/sol_modules.py:384-424).
+ * ------------------------------------------------------------------------ */
+
+/* Front: buf = lerp(buf, g, 1-beta); u = nesterov ? lerp(g, buf, beta) : buf
+ * (sol_modules.py:390-394). Writes d_u (S, r, c) bf16 in the original layout and
+ * per-matrix partial sums of bf16(u)^2 into d_partial (S * nparts floats, nparts
+ * from b2o_normuon_front_parts). dtype is the param/grad/momentum dtype. */
+int b2o_normuon_front_parts(int64_t rc);
+int b2o_normuon_front(const void* const* d_grads, void* const* d_bufs, int S, int r, int c,
+                      int dtype, float w_small, float w_large, int nesterov,
+                      uint16_t* d_u, float* d_partial, void* stream);
+
+/* Workspace needed by b2o_orthogonalize for a batch (bytes). */
+int64_t b2o_ortho_workspace_bytes(int S, int r, int c);
+
+/* Orthogonaliser (sol_modules.py:366-370; fallback 278-293).
+ *   mode 0 = quintic Newton-Schulz restated from the reference's fallback
+ *            (zeropower_via_newtonschulz5): coefficients[0..2] used every step;
+ *   mode 1 = Gram Newton-Schulz on the m x m Gram matrix with a per-step
+ *            coefficient table coeffs[3*T] and restart steps `resets`.
+ * d_u (S, r, c) bf16 is the front output (read only); d_partial is the front's
+ * sum-of-squares partials; the result o (S, r, c) bf16, original layout, goes to
+ * d_out, and per-row partial sums of o^2 go to d_rowsq (S * r * ceil(c/256)).
+ * norm_eps is added to the Frobenius norm; norm_safety multiplies it. */
+int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r, int c,
+                      int mode, const float* coeffs, int T, const int* resets, int nresets,
+                      float norm_eps, float norm_safety,
+                      void* d_ws, int64_t ws_bytes, uint16_t* d_out, float* d_rowsq,
+                      void* stream);
+
+/* Finish + apply (sol_modules.py:396-424): v_row lerp, row/matrix scaling,
+ * shape scale, cautious weight decay, update, bf16 mantissa split, EMA.
+ *   params/rems/emas/vrows: S pointers each (rems/emas may be NULL arrays)
+ *   param_dtype: B2O_F32 or B2O_BF16; rems non-NULL only for bf16 (bf16_master)
+ *   neg_lr = fp32(-lr); lr_wd = fp32(lr*wd) (cautious factor 1 - lr_wd*mask);
+ *   wd_factor = fp32(1 - lr*wd) (plain decay); wd_on, cautious flags;
+ *   shape_scale = fp32(sqrt(max(1, r/c))); w_beta2 = fp32(1-beta2);
+ *   ema_weight = fp32(1-decay)
+ *   d_scratch: S * (r + 4) floats of scratch. */
+int64_t b2o_normuon_apply_scratch_floats(int S, int r);
+int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c,
+                      void* const* params, uint16_t* const* rems, float* const* emas,
+                      float* const* vrows, int param_dtype,
+                      float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious,
+                      float shape_scale, float w_beta2, float ema_weight,
+                      float* d_scratch, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Batched bf16 GEMM on tcgen05 (exposed for tests and the micro-benchmark).
+ * D[b] = epilogue(op(A[b]) * op(B[b])), fp32 accumulation in tensor memory.
+ *   A is M x K: a_kmajor=1 -> stored row-major (M rows, K contiguous, lda);
+ *                a_kmajor=0 -> stored as K x M (M contiguous, lda).
+ *   B is N x K: b_kmajor=1 -> stored N rows with K contiguous (D = A * B^T);
+ *                b_kmajor=0 -> stored K x N (N contiguous, D = A * B).
+ *   epi: 0 = D = alpha * acc; 1 = D = alpha*I + beta*C + gamma*acc (P polynomial);
+ *        2 = D = bf16(bf16(beta*C) + bf16(gamma*bf16(acc)))  (quintic B);
+ *        3 = D = bf16(bf16(alpha*C) + bf16(acc))             (quintic X update).
+ *   sym: 1 -> output is symmetric, only tiles touching the upper triangle are
+ *        computed and each is mirrored (M must equal N).
+ *   d_scale: optional per-batch multiplier on acc (NULL = 1).
+ *   d_rowsq: optional per-row partial sums of bf16(D)^2, layout [b][tile_n][M].
+ * ------------------------------------------------------------------------ */
+int b2o_gemm_bf16(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor,
+                  const uint16_t* d_B, int64_t ldb, int64_t strideB, int b_kmajor,
+                  uint16_t* d_D, int64_t ldd, int64_t strideD,
+                  const uint16_t* d_C, int64_t ldc, int64_t strideC,
+                  int M, int N, int K, int batch, int epi, int sym,
+                  float alpha, float beta, float gamma, const float* d_scale,
+                  float* d_rowsq, void* stream);
+
+/* The same product on CUDA cores (no tensor cores, no mirroring); a test hook
+ * that checks the tensor-core path against an independent kernel. No
+ * reference counterpart. */
+int b2o_gemm_bf16_simt(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor,
+                       const uint16_t* d_B, int64_t ldb, int64_t strideB, int b_kmajor,
+                       uint16_t* d_D, int64_t ldd, int64_t strideD,
+                       const uint16_t* d_C, int64_t ldc, int64_t strideC,
+                       int M, int N, int K, int batch, int epi,
+                       float alpha, float beta, float gamma, const float* d_scale,
+                       float* d_rowsq, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2O_H_ */

@@ -1,0 +1,284 @@
+"""Parity of the engine's optimizer step with the oracle (the reference's own
+step restated on the CPU, pinned by tests/golden) and with torch's fused AdamW.
+
+Tolerances (stated where they are checked):
+  * AdamW / EMA element math: fp32 values within 2 ulp; bf16 values equal or
+    one bf16 ulp apart where the fp32 result sits on a rounding boundary.
+  * bf16 mantissa split / recombine: bit-exact given the same fp32 weight.
+  * Orthogonalised NorMuon updates: relative Frobenius error <= 1e-2 on the
+    cumulative update after 10 steps (bf16 Newton-Schulz is itself sensitive at
+    the 1e-2 level to GEMM accumulation order).
+"""
+import math
+
+import pytest
+import torch
+
+from oracle import gram_ns_ref, ref_step
+from sol_b200 import AdamW, EmaWeights, NorMuonGNS, _lib, build_optimizers, polar_express, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _ulp_f32(x):
+    return torch.finfo(torch.float32).eps * x.abs().clamp_min(torch.finfo(torch.float32).tiny)
+
+
+def assert_f32_ulps(a, b, ulps=2, what=""):
+    a, b = a.float().cpu(), b.float().cpu()
+    bad = (a - b).abs() > ulps * _ulp_f32(b) * 1.0001
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond {ulps} ulp; max |d| {(a - b).abs().max()}"
+
+
+def assert_bf16_close(a, b, what="", min_exact=0.999):
+    a, b = a.to(torch.bfloat16).cpu(), b.to(torch.bfloat16).cpu()
+    ai = a.view(torch.int16).int()
+    bi = b.view(torch.int16).int()
+    d = (ai - bi).abs()
+    assert d.max() <= 1, f"{what}: bf16 values more than one ulp apart"
+    assert (d == 0).float().mean() >= min_exact, f"{what}: too many 1-ulp differences"
+
+
+def rel_fro(a, b):
+    a, b = a.double().cpu(), b.double().cpu()
+    return (torch.linalg.norm(a - b) / torch.linalg.norm(b).clamp_min(1e-30)).item()
+
+
+# ------------------------------------------------------------------ AdamW ---
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_adamw_matches_torch_fused_cuda(cuda, dtype):
+    """Reference mode == torch.optim.AdamW(fused=True) on the same device."""
+    g = torch.Generator(device=cuda).manual_seed(0)
+    shapes = [(333, 77), (1024,), (5, 64, 32), (), (7,), (4096, 64)]
+    base = [torch.randn(s, generator=g, device=cuda) * 0.02 for s in shapes]
+    p1 = [torch.nn.Parameter(b.clone().to(dtype)) for b in base]
+    p2 = [torch.nn.Parameter(b.clone().to(dtype)) for b in base]
+    groups = lambda ps: [{"params": ps[:3], "lr": 2.4e-2, "weight_decay": 0.0},  # noqa: E731
+                         {"params": ps[3:5], "lr": 1e-2, "betas": (0.75, 0.95), "weight_decay": 0.1},
+                         {"params": ps[5:], "lr": 3e-3}]
+    ours = AdamW(groups(p1), betas=(0.9, 0.95), eps=1e-8, fused=True)
+    ref = torch.optim.AdamW(groups(p2), betas=(0.9, 0.95), eps=1e-8, fused=True)
+    for step in range(5):
+        for a, b in zip(p1, p2):
+            gr = (torch.randn(a.shape, generator=g, device=cuda) * 1e-3).to(dtype)
+            a.grad, b.grad = gr.clone(), gr.clone()
+        ours.step()
+        ref.step()
+    torch.cuda.synchronize()
+    for a, b in zip(p1, p2):
+        sa, sb = ours.state[a], ref.state[b]
+        if dtype == torch.float32:
+            assert_f32_ulps(a.data, b.data, what="param")
+            assert_f32_ulps(sa["exp_avg"], sb["exp_avg"], what="exp_avg")
+            assert_f32_ulps(sa["exp_avg_sq"], sb["exp_avg_sq"], what="exp_avg_sq")
+        else:
+            assert_bf16_close(a.data, b.data, "param")
+            assert_bf16_close(sa["exp_avg"], sb["exp_avg"], "exp_avg")
+            assert_bf16_close(sa["exp_avg_sq"], sb["exp_avg_sq"], "exp_avg_sq")
+    sd = ours.state_dict()
+    assert float(sd["state"][0]["step"]) == 5.0
+
+
+def test_adamw_master_mode_vs_oracle(cuda):
+    """bf16 params + bf16 remainder + fp32 moments + cautious decay vs the CPU restatement."""
+    g = torch.Generator().manual_seed(1)
+    shapes = [(512, 96), (1000,), (3, 40, 24)]
+    init = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    pg = [torch.nn.Parameter(x.to(torch.bfloat16).cuda()) for x in init]
+    pc = [torch.nn.Parameter(x.to(torch.bfloat16)) for x in init]
+    ours = AdamW(pg, lr=2.4e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, master="bf16_mt",
+                 cautious_wd=True)
+    orc = ref_step.MasterAdamW(pc, lr=2.4e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, cautious=True)
+    for step in range(6):
+        for a, b in zip(pg, pc):
+            gr = (torch.randn(b.shape, generator=g) * 1e-3)
+            gr[..., :3] *= 10
+            gr = gr.to(torch.bfloat16)
+            a.grad, b.grad = gr.cuda(), gr.clone()
+        ours.step()
+        orc.step()
+    torch.cuda.synchronize()
+    for a, b, st in zip(pg, pc, orc.state):
+        so = ours.state[a]
+        assert_f32_ulps(so["exp_avg"], st["m"], what="exp_avg")
+        assert_f32_ulps(so["exp_avg_sq"], st["v"], what="exp_avg_sq")
+        w_ours = a.data.float().cpu() + so["mant_rem"].float().cpu()
+        w_orc = b.data.float() + st["rem"].float()
+        assert_f32_ulps(w_ours, w_orc, ulps=2, what="reconstructed fp32 weight")
+
+
+def test_mantissa_split_is_bit_exact(cuda):
+    """p = bf16_RNE(w); rem = bf16_RNE(w - p) (sol_modules.py:423-424) for the same fp32 w.
+
+    With lr = 0 and no decay, AdamW leaves w unchanged, so one pass of the
+    kernel must reproduce torch's split of the reconstructed weight bit for bit."""
+    g = torch.Generator().manual_seed(2)
+    w = torch.randn(4099, generator=g) * 0.05
+    p0 = w.to(torch.bfloat16)
+    r0 = (w - p0.float()).to(torch.bfloat16)
+    p = torch.nn.Parameter(p0.clone().cuda())
+    opt = AdamW([p], lr=0.0, weight_decay=0.0, master="bf16_mt")
+    p.grad = torch.zeros_like(p)
+    opt._init_state(p)
+    opt.state[p]["mant_rem"].copy_(r0.cuda())
+    opt.step()
+    torch.cuda.synchronize()
+    wr = p0.float() + r0.float()
+    pe = wr.to(torch.bfloat16)
+    re = (wr - pe.float()).to(torch.bfloat16)
+    assert torch.equal(p.data.cpu().view(torch.int16), pe.view(torch.int16))
+    assert torch.equal(opt.state[p]["mant_rem"].cpu().view(torch.int16), re.view(torch.int16))
+
+
+# ----------------------------------------------------------------- NorMuon --
+def _normuon_pair(cfg, steps, cautious, bf16_master, orthogonalizer, coefficients="quintic", wd=0.1):
+    model_c = synth.SyntheticLM(cfg, seed=0)
+    model_g = synth.SyntheticLM(cfg, seed=0).cuda()
+    muon_c = [p for n, p in model_c.named_parameters() if n in ref_step.route(model_c.named_parameters())[0]]
+    names = ref_step.route(model_c.named_parameters())[0]
+    gmap = dict(model_g.named_parameters())
+    muon_g = [gmap[n] for n in names]
+    orc = ref_step.RefNorMuon(muon_c, lr=8e-3, weight_decay=wd, cautious_wd=cautious, bf16_master=bf16_master)
+    eng = NorMuonGNS(muon_g, lr=8e-3, weight_decay=wd, cautious_wd=cautious, bf16_master=bf16_master,
+                     orthogonalizer=orthogonalizer, coefficients=coefficients)
+    p0 = [p.detach().clone().float() for p in muon_c]
+    for it in range(steps):
+        mom = 0.85 + 0.10 * min(1.0, it / 300)
+        orc.group["momentum"] = mom
+        eng.param_groups[0]["momentum"] = mom
+        grads = synth.make_grads(model_c, it, seed=3)
+        gl = dict(zip([n for n, _ in model_c.named_parameters()], grads))
+        for n, p in zip(names, muon_c):
+            p.grad = gl[n]
+        for n, p in zip(names, muon_g):
+            p.grad = gl[n].cuda()
+        orc.step()
+        eng.step()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    return names, muon_c, muon_g, p0, orc, eng
+
+
+@pytest.mark.parametrize("cfg,cautious,mt", [(synth.C1, False, False), (synth.MICRO, True, True),
+                                              (synth.MICRO, False, False)])
+def test_normuon_quintic_matches_reference(cuda, cfg, cautious, mt):
+    names, pc, pg, p0, orc, eng = _normuon_pair(cfg, 10, cautious, mt, "quintic")
+    du_c = torch.cat([(p.detach().float() - a).reshape(-1) for p, a in zip(pc, p0)])
+    du_g = torch.cat([(p.detach().float().cpu() - a).reshape(-1) for p, a in zip(pg, p0)])
+    err = rel_fro(du_g, du_c)
+    print(f"{cfg.name}: cumulative update rel. Frobenius error after 10 steps = {err:.2e}")
+    assert err <= 1e-2
+    for i, (a, b) in enumerate(zip(pc, pg)):
+        e = rel_fro(b.detach().float().cpu() - p0[i], a.detach().float() - p0[i])
+        assert e <= 3e-2, f"{names[i]}: per-matrix update error {e:.3e}"
+        st_o, st_e = orc.state[i], eng.state[b]
+        # the momentum buffer does not depend on the orthogonaliser: same lerps
+        if a.dtype == torch.float32:
+            assert_f32_ulps(st_e["momentum_buffer"], st_o["momentum_buffer"], ulps=2, what="momentum")
+        else:
+            assert_bf16_close(st_e["momentum_buffer"], st_o["momentum_buffer"], "momentum", min_exact=0.99)
+        assert rel_fro(st_e["v_row"], st_o["v_row"]) < 3e-2
+
+
+def test_normuon_gram_quintic_table_matches_reference(cuda):
+    """Gram Newton-Schulz with the quintic table equals standard NS in exact arithmetic."""
+    names, pc, pg, p0, orc, eng = _normuon_pair(synth.MICRO, 10, True, True, "gram", "quintic")
+    du_c = torch.cat([(p.detach().float() - a).reshape(-1) for p, a in zip(pc, p0)])
+    du_g = torch.cat([(p.detach().float().cpu() - a).reshape(-1) for p, a in zip(pg, p0)])
+    err = rel_fro(du_g, du_c)
+    print(f"gram/quintic: cumulative update rel. Frobenius error after 10 steps = {err:.2e}")
+    assert err <= 1e-2
+
+
+@pytest.mark.parametrize("r,c", [(256, 256), (768, 256), (256, 1408), (1024, 1024), (8, 128)])
+def test_gram_polar_express_vs_fp64_restatement(cuda, r, c):
+    g = torch.Generator().manual_seed(r + c)
+    U = (torch.randn(3, r, c, generator=g) * 1e-3).to(torch.bfloat16)
+    opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=cuda))], orthogonalizer="gram",
+                     coefficients="polar_express")
+    out = opt._orthogonalize_batch(U.cuda(), 5)
+    torch.cuda.synchronize()
+    ref64 = gram_ns_ref.gram_ns(U, polar_express.polar_express(5), safety=opt.norm_safety)
+    err = rel_fro(out.float(), ref64)
+    print(f"({r},{c}) gram/PE vs fp64: {err:.3e}")
+    assert err < 0.12
+    pf = gram_ns_ref.polar_factor(U)
+    assert rel_fro(out.float(), pf) < 0.25
+
+
+# -------------------------------------------------------------- full step --
+def test_full_step_with_ema_matches_reference(cuda):
+    """build_optimizers + EmaWeights (folded into the passes) vs the oracle's
+    muon -> adamw -> ema step on the MICRO recipe set, 6 steps."""
+    cfg = synth.MICRO
+    kw = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+    mc = synth.SyntheticLM(cfg, seed=0)
+    mg = synth.SyntheticLM(cfg, seed=0).cuda()
+    ref = ref_step.RefStep(mc, **kw)
+    muon, adamw = build_optimizers(mg, orthogonalizer="quintic", **kw)
+    ema = EmaWeights(mg, 0.999)
+    p0 = [p.detach().clone().float() for p in mc.parameters()]
+    for it in range(6):
+        frac = (it + 1) / 5
+        ref.muon.group["lr"] = ref.muon.group["base_lr"] * frac
+        for gg in ref.adamw.param_groups:
+            gg["lr"] = gg["base_lr"] * frac
+        for opt in (muon, adamw):
+            for gg in opt.param_groups:
+                gg["lr"] = gg["base_lr"] * frac
+        grads = synth.make_grads(mc, it, seed=0)
+        synth.set_grads(mc, grads)
+        synth.set_grads(mg, [x.cuda() for x in grads])
+        ref.step()
+        muon.step()
+        adamw.step()
+        ema.update()
+    torch.cuda.synchronize()
+    assert ema._armed and ema._folded == set()
+    named_c = list(mc.named_parameters())
+    named_g = dict(mg.named_parameters())
+    muon_names = set(ref_step.route(named_c)[0])
+    for i, (n, pcpu) in enumerate(named_c):
+        pgpu = named_g[n]
+        if n in muon_names:
+            e = rel_fro(pgpu.detach().float().cpu() - p0[i], pcpu.detach().float() - p0[i])
+            assert e < 3e-2, f"{n}: {e}"
+        else:
+            assert_bf16_close(pgpu.data, pcpu.data, n, min_exact=0.995)
+            ms, mo = adamw.state[pgpu], ref.adamw.state[pcpu]
+            assert_bf16_close(ms["exp_avg"], mo["exp_avg"], n + "/exp_avg", min_exact=0.995)
+        # EMA: lerp of each step's params; differences only through the params themselves
+        sh_g = ema.shadow[i].cpu()
+        sh_c = ref.shadow[i]
+        assert rel_fro(sh_g - p0[i], sh_c - p0[i]) < 3e-2 or torch.equal(sh_g, sh_c)
+
+
+def test_ema_folded_equals_standalone(cuda):
+    cfg = synth.MICRO
+    m1 = synth.SyntheticLM(cfg, seed=0).cuda()
+    m2 = synth.SyntheticLM(cfg, seed=0).cuda()
+    kw = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+    o1 = build_optimizers(m1, **kw)
+    o2 = build_optimizers(m2, **kw)
+    e1 = EmaWeights(m1, 0.99)
+    e2 = EmaWeights(m2, 0.99, fuse=False)
+    for it in range(4):
+        grads = synth.make_grads(m1, it, seed=5)
+        synth.set_grads(m1, grads)
+        synth.set_grads(m2, [x.clone() for x in grads])
+        for o in o1:
+            o.step()
+        e1.update()
+        for o in o2:
+            o.step()
+        e2.update()
+    torch.cuda.synchronize()
+    for a, b in zip(e1.shadow, e2.shadow):
+        assert_f32_ulps(a, b, ulps=0, what="ema")
+    # averaged(): params become bf16(shadow) and are restored afterwards
+    before = [p.detach().clone() for p in m1.parameters()]
+    with e1.averaged():
+        for p, s in zip(m1.parameters(), e1.shadow):
+            assert torch.equal(p.data, s.to(p.dtype))
+    for p, b in zip(m1.parameters(), before):
+        assert torch.equal(p.data, b)

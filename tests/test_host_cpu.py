@@ -1,0 +1,163 @@
+"""Host-side logic that needs no GPU: routing, coefficient tables, the C ABI
+library's exports, and the no-CPU-fallback rule."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import gram_ns_ref, ref_step
+from sol_b200 import _lib, polar_express, synth
+from sol_b200.routing import route_params
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+# ------------------------------------------------------------------ routing --
+@pytest.mark.parametrize("cfg", [synth.C1, synth.MICRO, synth.C2, synth.C5])
+def test_routing_matches_reference(cfg):
+    model = synth.SyntheticLM(cfg, device="meta")
+    named = list(model.named_parameters())
+    ours = route_params(named)
+    ids = {id(p): n for n, p in named}
+    ours_names = tuple([ids[id(p)] for p in group] for group in ours)
+    assert ours_names == ref_step.route(named)
+
+
+def test_c2_routing_counts():
+    """L14 recipe: 14 x 5 NorMuon matrices (incl. the 8x1024 attention gate),
+    7 vocabulary tables (embedding, second embedding, 5 value embeddings)."""
+    model = synth.SyntheticLM(synth.C2, device="meta")
+    muon, embed, norm, ve = route_params(model.named_parameters())
+    assert len(muon) == 14 * 5
+    shapes = sorted({tuple(p.shape) for p in muon})
+    assert shapes == [(8, 1024), (1024, 1024), (1024, 5632), (3072, 1024), (5632, 1024)]
+    assert sum(p.numel() for p in muon) == 14 * (3072 * 1024 + 1024 * 1024 + 8 * 1024 + 2 * 5632 * 1024)
+    assert sum(p.numel() for p in embed) == 2 * 32768 * 1024
+    assert ve[0].shape == (5, 32768, 1024)
+    assert all(p.numel() < 100_000 for p in norm)
+
+
+# ----------------------------------------------------------- coefficients --
+def test_polar_express_table_properties():
+    table = polar_express.polar_express(5)
+    assert len(table) == 5
+    # composition maps [1e-3, 1] into a narrow band around 1 ...
+    xs = [10 ** (-3 + 3 * i / 400) for i in range(401)]
+    ys = [polar_express.apply_table(table, x) for x in xs]
+    assert 0.8 < min(ys) and max(ys) < 1.2
+    # ... much tighter than the quintic constant iteration
+    yq = [polar_express.apply_table([polar_express.QUINTIC] * 5, x) for x in xs]
+    assert (max(ys) - min(ys)) < 0.5 * (max(yq) - min(yq))
+    # each step is centred on 1 over its interval (recentred minimax)
+    lo, hi = 1e-3, 1.0
+    for coef in table:
+        pl, pu = polar_express._poly(coef, lo), polar_express._poly(coef, hi)
+        assert abs((pl + pu) / 2 - 1) < 1e-12
+        lo, hi = pl, pu
+
+
+def test_remez_equioscillation():
+    a, b, c, E = polar_express.optimal_odd_quintic(0.1, 1.0)
+    f = lambda x: 1 - (a * x + b * x ** 3 + c * x ** 5)  # noqa: E731
+    xs = [0.1 + 0.9 * i / 20000 for i in range(20001)]
+    worst = max(abs(f(x)) for x in xs)
+    assert worst <= abs(E) * (1 + 1e-9)
+    assert abs(abs(f(0.1)) - abs(E)) < 1e-12 and abs(abs(f(1.0)) - abs(E)) < 1e-12
+
+
+# ------------------------------------------------------- Gram schedule math --
+def test_gram_schedule_equals_standard_ns_in_exact_arithmetic():
+    """With the same coefficients, the Gram iteration (with restarts) equals the
+    quintic iteration X <- aX + b(XX^T)X + c(XX^T)^2 X in float64."""
+    g = torch.Generator().manual_seed(0)
+    U = torch.randn(3, 24, 40, generator=g, dtype=torch.float64)
+    table = [polar_express.QUINTIC] * 5
+    out = gram_ns_ref.gram_ns(U, table, resets=(2,), eps=0.0)
+    ref = []
+    for u in U:
+        X = u / torch.linalg.norm(u)
+        for a, b, c in table:
+            A = X @ X.t()
+            X = a * X + (b * A + c * A @ A) @ X
+        ref.append(X)
+    torch.testing.assert_close(out, torch.stack(ref), rtol=1e-9, atol=1e-11)
+    # tall inputs are iterated as their transpose
+    Ut = U.transpose(1, 2).contiguous()
+    torch.testing.assert_close(gram_ns_ref.gram_ns(Ut, table, eps=0.0), out.transpose(1, 2), rtol=1e-9, atol=1e-11)
+
+
+def test_polar_express_gram_approaches_polar_factor():
+    g = torch.Generator().manual_seed(1)
+    U = torch.randn(2, 32, 64, generator=g, dtype=torch.float64)
+    out = gram_ns_ref.gram_ns(U, polar_express.polar_express(5), safety=1.01)
+    pf = gram_ns_ref.polar_factor(U)
+    s = torch.linalg.svdvals(out)
+    assert s.min() > 0.6 and s.max() < 1.25
+    rel = torch.linalg.norm(out - pf) / torch.linalg.norm(pf)
+    assert rel < 0.2
+
+
+# ------------------------------------------------------------------- C ABI --
+def _header_symbols():
+    text = (ROOT / "include" / "b2o.h").read_text()
+    return sorted(set(re.findall(r"\b(b2o_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert set(_header_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = _lib.load()
+    for name in _header_symbols():
+        assert hasattr(lib, name), name
+    assert lib.b2o_version() == 1
+    assert lib.b2o_normuon_front_parts(16384) == 1
+    assert lib.b2o_ortho_workspace_bytes(14, 5632, 1024) > 0
+    assert lib.b2o_ortho_workspace_bytes(0, 1, 1) == -1
+
+
+def test_host_validation_without_gpu():
+    """Invalid arguments are rejected on the host (nothing launched)."""
+    lib = _lib.load()
+    rc = lib.b2o_normuon_front(None, None, 0, 4, 4, 1, 0.05, 0.95, 1, None, None, None)
+    assert rc < 0 and "1..64" in _lib.last_error()
+    rc = lib.b2o_adamw_step(None, 0, None, 0, 1, 1, 0.0, None)
+    assert rc < 0
+    rc = lib.b2o_orthogonalize(None, None, 1, 4, 4, 0, None, 5, None, 0, 1e-7, 1.0, None, 0, None, None, None)
+    assert rc < 0 and "bad arguments" in _lib.last_error()
+
+
+def test_no_cpu_fallback():
+    from sol_b200 import NorMuonGNS, AdamW, EmaWeights
+    p = torch.nn.Parameter(torch.randn(16, 8))
+    p.grad = torch.randn(16, 8)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        NorMuonGNS([p]).step()
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        AdamW([p]).step()
+    m = torch.nn.Linear(4, 4)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        EmaWeights(m).update()
+
+
+def test_adamw_state_dict_layout_matches_torch():
+    from sol_b200 import AdamW
+    params = [torch.nn.Parameter(torch.randn(4, 4))]
+    ours = AdamW(params, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, fused=True)
+    ref = torch.optim.AdamW(params, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, fused=True)
+    assert set(ours.state_dict()["param_groups"][0]) == set(ref.state_dict()["param_groups"][0])
+
+
+def test_normuon_param_group_keys_match_reference():
+    from sol_b200 import NorMuonGNS
+    p = torch.nn.Parameter(torch.randn(4, 4))
+    keys = set(NorMuonGNS([p]).state_dict()["param_groups"][0])
+    assert keys == {"lr", "momentum", "beta2", "nesterov", "ns_steps", "weight_decay", "params"}
+
+
+def test_ctypes_structs_match_header_layout():
+    assert ctypes.sizeof(_lib.AdamwTensor) == 6 * 8 + 8 + 4 + 4
+    assert ctypes.sizeof(_lib.AdamwGroup) == 8 * 4
