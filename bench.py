@@ -1,0 +1,414 @@
+#!/usr/bin/env python
+"""Optimizer-step benchmark (BASELINE.json metric: NorMuon+AdamW step ms, L14 d1024).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl engine|reference] [--device cpu|cuda]
+
+engine arm (default): the L14/d1024/d_ff 5632/V 32768 recipe parameter set
+on seeded synthetic bf16 tensors resident in HBM; one
+step = muon.step(); adamw.step(); ema.update() through the drop-in API
+(build_optimizers + EmaWeights). Prints one JSON line with the step time, the
+Gram Newton-Schulz GEMM roofline, the end-to-end time through the same API
+with host gradients copied in and a result read back, and the CPU baseline.
+With N > 1 (torchrun), the step is sharded by matrices / table rows and the
+updated bf16 weights are all-gathered with NCCL; time = max over ranks.
+
+reference arm: the reference's own optimizer math (the CPU oracle, bit-exact
+with transformer_lm.sol_modules on CPU) on the host cores, on a 1/14 sample of
+the same workload (one layer's matrices and 1/14 of every vocabulary table)
+scaled to a full step. ``--device cuda`` runs the same torch code on the GPU
+over the full workload (the reference's GPU step with its quintic fallback).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "cs336-a1-sol_b200"))
+
+from sol_b200 import EmaWeights, _lib, build_optimizers, synth  # noqa: E402
+from sol_b200.sharding import ShardedStep  # noqa: E402
+
+RECIPE = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+MOM_WARMUP = 300
+# dram__bytes_read.sum + dram__bytes_write.sum of one Gram-NS GEMM launch list,
+# from profiles/ (None until a capture exists for the current kernel).
+GEMM_TRAFFIC_BYTES_PER_STEP = None
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gram_flops(m, n, T=5, resets=(2,), mode="gram"):
+    """Algorithmic FLOPs of the orthogonaliser's GEMM list for one matrix
+    (symmetric outputs counted at half of the dense product)."""
+    if mode == "quintic":
+        return T * (m * m * n + m ** 3 + 2 * m * m * n)
+    f = m * m * n  # first Gram matrix
+    q_is_identity = True
+    for t in range(T):
+        if t > 0 and t in resets:
+            f += 2 * m * m * n + m * m * n  # X = Q X, R = X X^T
+            q_is_identity = True
+        f += m ** 3  # R^2 (symmetric)
+        if not q_is_identity:
+            f += 2 * m ** 3
+        q_is_identity = False
+        if t < T - 1 and (t + 1) not in resets:
+            f += 3 * m ** 3  # P R (full) and (P R) P (symmetric)
+    return f + 2 * m * m * n  # out = Q X
+
+
+def step_flops(model, muon, mode):
+    tot = 0
+    for g in muon.param_groups:
+        for p in g["params"]:
+            if muon._owned is not None and id(p) not in muon._owned:
+                continue
+            r, c = p.shape
+            tot += gram_flops(min(r, c), max(r, c), mode=mode)
+    return tot
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if args.device == "cuda" else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif args.device == "cuda":
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------- CPU legs ---
+def sample_config(cfg):
+    """One layer of cfg with 1/L of every vocabulary table: 1/L of a full step."""
+    from dataclasses import replace
+    return replace(cfg, name=cfg.name + "_sample", n_layers=1, vocab=cfg.vocab // cfg.n_layers)
+
+
+def run_oracle_steps(cfg, device, steps, warmup, threads=None):
+    from oracle import ref_step  # the checker / reference arm only
+    if threads:
+        torch.set_num_threads(threads)
+    model = synth.SyntheticLM(cfg, device=device, seed=0)
+    grads = synth.make_grads(model, 0, seed=0)
+    synth.set_grads(model, grads)
+    step = ref_step.RefStep(model, **RECIPE)
+    times = []
+    for it in range(warmup + steps):
+        mom = 0.85 + 0.10 * min(1.0, it / MOM_WARMUP)
+        step.muon.group["momentum"] = mom
+        if device == "cuda":
+            torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        step.step()
+        if device == "cuda":
+            torch.cuda.synchronize()
+        if it >= warmup:
+            times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times), times
+
+
+def cpu_baseline(cfg, steps=2, warmup=1):
+    scfg = sample_config(cfg)
+    threads = os.cpu_count() or 1
+    ms, _ = run_oracle_steps(scfg, "cpu", steps, warmup, threads)
+    return {"value": ms * cfg.n_layers, "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"one layer of {cfg.name} (5 NorMuon matrices) + 1/{cfg.n_layers} of every vocabulary "
+                      f"table, median of {steps} steps after {warmup} warm-up, scaled x{cfg.n_layers}"}
+
+
+def reference_arm(args, world, rank):
+    cfg = synth.CONFIGS[args.config]
+    if rank != 0:
+        return None
+    if args.device == "cuda":
+        ms, _ = run_oracle_steps(cfg, "cuda", min(args.steps, 10), max(1, min(args.warmup, 3)))
+        line = {"metric": "optimizer step ms (NorMuon+AdamW+EMA)", "value": ms, "unit": "ms", "impl": "reference",
+                "device": "cuda", "n_gpus": 1, "steps": min(args.steps, 10), "higher_is_better": False,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfg.name, "orthogonalizer": "quintic fallback (torch bf16 matmul)"},
+                "note": "reference optimizer math (bit-exact CPU oracle) executed with torch on the GPU"}
+        line["e2e"] = {"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+        return line
+    steps, warm = min(args.steps, 3), min(args.warmup, 1)
+    scfg = sample_config(cfg)
+    ms, _ = run_oracle_steps(scfg, "cpu", steps, warm, os.cpu_count() or 1)
+    value = ms * cfg.n_layers
+    cb = {"value": value, "unit": "ms", "cores": torch.get_num_threads(), "kind": "port",
+          "sample": f"one layer of {cfg.name} + 1/{cfg.n_layers} of every vocabulary table, median of {steps} "
+                    f"steps after {warm} warm-up, scaled x{cfg.n_layers}"}
+    return {"metric": "optimizer step ms (NorMuon+AdamW+EMA)", "value": value, "unit": "ms", "impl": "reference",
+            "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": value, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "orthogonalizer": "quintic fallback (reference, GNS absent)"},
+            "cpu_baseline": cb, "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
+# ------------------------------------------------------------ engine arm ---
+def engine_arm(args, world, rank, local):
+    cfg = synth.CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    _lib.load()
+    model = synth.SyntheticLM(cfg, device=dev, seed=0)
+    named = list(model.named_parameters())
+    # gradients live in one flat buffer so the end-to-end leg copies them in with one H2D copy
+    total = sum(p.numel() for _, p in named)
+    flat_grad = torch.empty(total, dtype=cfg.dtype, device=dev)
+    grads = synth.make_grads(model, 0, seed=0)
+    off = 0
+    for (_, p), g in zip(named, grads):
+        n = p.numel()
+        view = flat_grad[off:off + n].view_as(p)
+        view.copy_(g)
+        p.grad = view
+        off += n
+    del grads
+    muon, adamw = build_optimizers(model, orthogonalizer=args.orthogonalizer, coefficients=args.coefficients,
+                                   adam_master="bf16_mt", **RECIPE)
+    ema = EmaWeights(model, 0.999)
+    sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank) if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+    ortho_events = []
+    muon._timing_events = ortho_events
+    adam_ev = []
+
+    def one_step(it, record=False):
+        mom = 0.85 + 0.10 * min(1.0, it / MOM_WARMUP)
+        for g in muon.param_groups:
+            g["momentum"] = mom
+        muon.step()
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        adamw.step()
+        if record:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            adam_ev.append((e0, e1))
+        ema.update()
+        if sharded is not None:
+            sharded.gather()
+
+    for it in range(args.warmup):
+        one_step(it)
+    torch.cuda.synchronize()
+    ortho_events.clear()
+    barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = _lib.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(args.steps):
+        one_step(args.warmup + k, record=True)
+    end.record(stream)
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    clocks = sampler.stop()
+    err = _lib.device_error()
+    if err:
+        raise RuntimeError(f"device error word {err}")
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world, dev)
+    ortho_ms = sum(a.elapsed_time(b) for a, b in ortho_events) / args.steps
+    adam_ms = sum(a.elapsed_time(b) for a, b in adam_ev) / args.steps
+    mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
+    flops = step_flops(model, muon, mode)
+    peak_tf, peak_gbs, peak_kind = peaks()
+    achieved = flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None
+    # AdamW+EMA streaming bytes: p 2+2, rem 2+2, g 2, m 4+4, v 4+4, fp32 EMA 4+4 = 34 B/elem
+    adam_elems = sum(p.numel() for g in adamw.param_groups for p in g["params"])
+    adam_bytes = adam_elems * 34 / (world if sharded else 1)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev)
+    line = {
+        "metric": "optimizer step ms (NorMuon+AdamW+EMA)", "value": ms, "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg.name, "params": total, "muon_matrices": sum(len(g["params"]) for g in
+                                                                            muon.param_groups),
+                   "orthogonalizer": f"{args.orthogonalizer}/{args.coefficients if mode == 'gram' else 'quintic'}",
+                   "adamw": "bf16 + bf16 remainder, fp32 moments", "ema": "fp32, folded",
+                   "l2": "working set > L2 (126 MB); no flush",
+                   "parallelism": f"shard{world}" if world > 1 else "single"},
+        "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
+                      "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
+        "adamw_gbs": adam_bytes / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else None,
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (Gram Newton-Schulz GEMM list)",
+                     "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": (achieved / peak_tf) if achieved else None,
+                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP, "flops_per_step": flops,
+                     "peak_kind": f"{peak_kind} bf16 burst"},
+        "clocks": clocks, "gpu_launches": launches,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg)
+    return line
+
+
+def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev):
+    """Same step through the public API, with the step's gradients copied in
+    from pinned host memory and a result read back every step."""
+    host = torch.empty(flat_grad.numel(), dtype=flat_grad.dtype, pin_memory=True)
+    host.copy_(flat_grad.cpu())
+    probe = next(iter(muon.param_groups[0]["params"]))
+    out = torch.empty(256, dtype=probe.dtype, pin_memory=True)
+    stream = torch.cuda.current_stream(dev)
+    for it in range(2):
+        flat_grad.copy_(host, non_blocking=True)
+        one_step(it)
+        out.copy_(probe.detach().reshape(-1)[:256], non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for k in range(args.steps):
+        flat_grad.copy_(host, non_blocking=True)
+        one_step(k)
+        out.copy_(probe.detach().reshape(-1)[:256], non_blocking=True)
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / args.steps, world, dev)
+    return {"value": ms, "unit": "ms", "h2d_bytes_per_step": host.numel() * host.element_size(),
+            "d2h_bytes_per_step": out.numel() * out.element_size()}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--device", choices=["cuda", "cpu"], default=None,
+                    help="engine: cuda; reference arm: cpu (host cores) unless cuda is given")
+    ap.add_argument("--config", default="c2_L14_d1024", choices=sorted(synth.CONFIGS))
+    ap.add_argument("--orthogonalizer", default="gram", choices=["gram", "quintic"])
+    ap.add_argument("--coefficients", default="polar_express", choices=["polar_express", "quintic"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.device is None:
+        args.device = "cuda" if args.impl == "engine" else "cpu"
+    if args.warmup < 3 and args.impl == "engine":
+        args.warmup = 3
+    if args.impl == "reference" and args.device == "cpu":
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        if rank == 0:
+            print(json.dumps(reference_arm(args, world, rank)), flush=True)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            line = reference_arm(args, world, rank)
+        else:
+            line = engine_arm(args, world, rank, local)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

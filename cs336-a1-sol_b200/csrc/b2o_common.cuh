@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include <atomic>
@@ -39,6 +40,12 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+// IEEE binary16 stored as raw bits (round-to-nearest-even).
+__device__ __forceinline__ float f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f32_to_f16(float f) { return __half_as_ushort(__float2half_rn(f)); }
+// 16-bit storage of either kind: half != 0 selects binary16, else bfloat16.
+__device__ __forceinline__ float h16_to_f32(uint16_t h, int half) { return half ? f16_to_f32(h) : bf16_to_f32(h); }
+__device__ __forceinline__ uint16_t f32_to_h16(float f, int half) { return half ? f32_to_f16(f) : f32_to_bf16(f); }
 
 // torch's lerp (ATen/native/Lerp.h): small weights interpolate from `self`,
 // large ones from `end`; evaluated in fp32 opmath with fused multiply-add.

@@ -33,6 +33,7 @@ struct Operand {
   int64_t ld;       // elements between consecutive stored rows
   int64_t stride;   // elements between batch entries
   int kmajor;       // 1: stored [i][k] (k contiguous); 0: stored [k][i] (i contiguous)
+  int half;         // element type: 0 = bfloat16, 1 = binary16 (A and B must agree)
 };
 struct Epilogue {
   int kind;          // 0 scale, 1 poly (alpha*I + beta*C + gamma*acc), 2 quintic-B, 3 quintic-X
@@ -42,6 +43,7 @@ struct Epilogue {
   int64_t ldc, strideC;
   uint16_t* D;
   int64_t ldd, strideD;
+  int d_half;          // D (and C) element type: 0 = bfloat16, 1 = binary16
   float* rowsq;        // per-row partial sums of bf16(D)^2: [b][tile_n (256 wide)][M]
 };
 int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch,

@@ -141,17 +141,29 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
                        static_cast<cudaStream_t>(stream));
 }
 
-int b2o_gemm_bf16(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B, int64_t ldb,
-                  int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD, const uint16_t* d_C,
-                  int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int epi, int sym, float alpha,
-                  float beta, float gamma, const float* d_scale, float* d_rowsq, void* stream) {
-  Operand A{d_A, lda, strideA, a_kmajor ? 1 : 0};
-  Operand B{d_B, ldb, strideB, b_kmajor ? 1 : 0};
+int b2o_gemm(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B, int64_t ldb,
+             int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD, const uint16_t* d_C,
+             int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int in_dtype, int out_dtype, int epi, int sym,
+             float alpha, float beta, float gamma, const float* d_scale, float* d_rowsq, void* stream) {
+  if ((in_dtype != B2O_BF16 && in_dtype != B2O_F16) || (out_dtype != B2O_BF16 && out_dtype != B2O_F16)) {
+    set_error("gemm: dtypes must be B2O_BF16 or B2O_F16"); return -1;
+  }
+  Operand A{d_A, lda, strideA, a_kmajor ? 1 : 0, in_dtype == B2O_F16};
+  Operand B{d_B, ldb, strideB, b_kmajor ? 1 : 0, in_dtype == B2O_F16};
   Epilogue e;
   memset(&e, 0, sizeof(e));
   e.kind = epi; e.alpha = alpha; e.beta = beta; e.gamma = gamma; e.scale = d_scale;
   e.C = d_C; e.ldc = ldc; e.strideC = strideC; e.D = d_D; e.ldd = ldd; e.strideD = strideD; e.rowsq = d_rowsq;
+  e.d_half = out_dtype == B2O_F16;
   return gemm(A, B, e, M, N, K, batch, sym, static_cast<cudaStream_t>(stream));
+}
+
+int b2o_gemm_bf16(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B, int64_t ldb,
+                  int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD, const uint16_t* d_C,
+                  int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int epi, int sym, float alpha,
+                  float beta, float gamma, const float* d_scale, float* d_rowsq, void* stream) {
+  return b2o_gemm(d_A, lda, strideA, a_kmajor, d_B, ldb, strideB, b_kmajor, d_D, ldd, strideD, d_C, ldc, strideC, M,
+                  N, K, batch, B2O_BF16, B2O_BF16, epi, sym, alpha, beta, gamma, d_scale, d_rowsq, stream);
 }
 
 /* Test hook: the same GEMM on the CUDA-core path (no tensor cores). */

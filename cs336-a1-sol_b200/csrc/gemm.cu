@@ -39,7 +39,7 @@ constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct Params {
   int M, N, K, batch;
-  int a_kmajor, b_kmajor, sym;
+  int a_kmajor, b_kmajor, sym, in_half;
   int tiles_m, tiles_n, tiles_per_batch, total_tiles, nk;
   Epilogue e;
   int* err;
@@ -166,7 +166,7 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& b, int&
 
 // ----------------------------------------------------------- epilogue ------
 __device__ __forceinline__ void load_row32(const uint16_t* base, int64_t ld, int row, int col0, int M, int N,
-                                           bool vec, float* out) {
+                                           bool vec, int half, float* out) {
   if (vec) {
     const uint4* src = reinterpret_cast<const uint4*>(base + static_cast<int64_t>(row) * ld + col0);
 #pragma unroll
@@ -175,15 +175,15 @@ __device__ __forceinline__ void load_row32(const uint16_t* base, int64_t ld, int
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        out[q * 8 + 2 * h] = bf16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu));
-        out[q * 8 + 2 * h + 1] = bf16_to_f32(static_cast<uint16_t>(w[h] >> 16));
+        out[q * 8 + 2 * h] = h16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu), half);
+        out[q * 8 + 2 * h + 1] = h16_to_f32(static_cast<uint16_t>(w[h] >> 16), half);
       }
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int col = col0 + j;
-      out[j] = (row < M && col < N) ? bf16_to_f32(base[static_cast<int64_t>(row) * ld + col]) : 0.f;
+      out[j] = (row < M && col < N) ? h16_to_f32(base[static_cast<int64_t>(row) * ld + col], half) : 0.f;
     }
   }
 }
@@ -286,7 +286,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer ---
     if (lane == 0) {
-      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(!p.a_kmajor) << 15) |
+      const uint32_t fmt = p.in_half ? 0u : 1u;  // kind::f16 operand format: 0 = f16, 1 = bf16
+      const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(!p.a_kmajor) << 15) |
                              (static_cast<uint32_t>(!p.b_kmajor) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
                              (static_cast<uint32_t>(BM >> 4) << 24);
       const uint32_t a_lbo = p.a_kmajor ? 16u : 8192u;
@@ -357,13 +358,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (col0 < p.N && row < p.M) {
           const bool full = col0 + 32 <= p.N;
           float cv[32];
-          if (e.kind != 0) load_row32(Cb, e.ldc, row, col0, p.M, p.N, vec_c && full, cv);
+          if (e.kind != 0) load_row32(Cb, e.ldc, row, col0, p.M, p.N, vec_c && full, e.d_half, cv);
           uint16_t out[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float x = epi_value(p, e.kind, v[j], e.kind != 0 ? cv[j] : 0.f, sc, row, col0 + j);
-            out[j] = f32_to_bf16(x);
-            const float xr = bf16_to_f32(out[j]);
+            out[j] = f32_to_h16(x, e.d_half);
+            const float xr = h16_to_f32(out[j], e.d_half);
             if (col0 + j < p.N) rsq = fmaf(xr, xr, rsq);
           }
           if (!p.sym) {
@@ -443,7 +444,7 @@ static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batc
   }
   dims[2] = batch; box[2] = 1;
   if (batch == 1) strides[1] = strides[0] * dims[1];  // any valid stride
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(op.ptr), dims, strides, box, estr,
+  CUresult r = fn(map, op.half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(op.ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -465,14 +466,14 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(Operand A, Operand B, Ep
   float acc = 0.f;
   if (col < N) {
     for (int k = 0; k < K; ++k) {
-      const float a = bf16_to_f32(A.kmajor ? Ab[static_cast<int64_t>(row) * A.ld + k] : Ab[static_cast<int64_t>(k) * A.ld + row]);
-      const float bb = bf16_to_f32(B.kmajor ? Bb[static_cast<int64_t>(col) * B.ld + k] : Bb[static_cast<int64_t>(k) * B.ld + col]);
+      const float a = h16_to_f32(A.kmajor ? Ab[static_cast<int64_t>(row) * A.ld + k] : Ab[static_cast<int64_t>(k) * A.ld + row], A.half);
+      const float bb = h16_to_f32(B.kmajor ? Bb[static_cast<int64_t>(col) * B.ld + k] : Bb[static_cast<int64_t>(k) * B.ld + col], B.half);
       acc = fmaf(a, bb, acc);
     }
   }
   float sq = 0.f;
   if (col < N) {
-    const float c = E.C ? bf16_to_f32(E.C[static_cast<int64_t>(b) * E.strideC + static_cast<int64_t>(row) * E.ldc + col]) : 0.f;
+    const float c = E.C ? h16_to_f32(E.C[static_cast<int64_t>(b) * E.strideC + static_cast<int64_t>(row) * E.ldc + col], E.d_half) : 0.f;
     float x;
     switch (E.kind) {
       case 0: x = acc * (E.scale ? E.alpha * E.scale[b] : E.alpha); break;
@@ -480,9 +481,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(Operand A, Operand B, Ep
       case 2: x = round_bf16(round_bf16(E.beta * c) + round_bf16(E.gamma * round_bf16(acc))); break;
       default: x = round_bf16(round_bf16(E.alpha * c) + round_bf16(acc)); break;
     }
-    const uint16_t o = f32_to_bf16(x);
+    const uint16_t o = f32_to_h16(x, E.d_half);
     E.D[static_cast<int64_t>(b) * E.strideD + static_cast<int64_t>(row) * E.ldd + col] = o;
-    const float xr = bf16_to_f32(o);
+    const float xr = h16_to_f32(o, E.d_half);
     sq = xr * xr;
   }
   if (E.rowsq) {
@@ -527,12 +528,16 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   if (E.kind != 0 && !E.C) { set_error("gemm: epilogue needs C"); return -1; }
   if (sym && M != N) { set_error("gemm: symmetric output needs M == N"); return -1; }
   if (sym && E.rowsq) { set_error("gemm: row sums are not produced for symmetric outputs"); return -1; }
+  if (A.half != B.half) { set_error("gemm: A and B must have the same element type"); return -1; }
+  if ((E.kind == 2 || E.kind == 3) && (E.d_half || A.half)) {
+    set_error("gemm: the quintic epilogues restate bf16 arithmetic and need bf16 data"); return -1;
+  }
   if (!gemm_tc_supported(A, B, E, M, N, K)) return gemm_simt(A, B, E, M, N, K, batch, stream);
 
   tc::Params p;
   memset(&p, 0, sizeof(p));
   p.M = M; p.N = N; p.K = K; p.batch = batch;
-  p.a_kmajor = A.kmajor; p.b_kmajor = B.kmajor; p.sym = sym;
+  p.a_kmajor = A.kmajor; p.b_kmajor = B.kmajor; p.sym = sym; p.in_half = A.half;
   p.tiles_m = (M + tc::BM - 1) / tc::BM;
   p.tiles_n = (N + tc::BN - 1) / tc::BN;
   if (sym) {

@@ -17,7 +17,9 @@
 //       P_t = a_t I + b_t R + c_t R^2;  Q <- Q P_t;  R <- P_t R P_t
 //       and form X_T = Q X0 only at restarts and at the end. At a restart step
 //       the iterate X = Q X0 is materialised and R recomputed from it, which
-//       bounds the drift between Q and R accumulated in bf16.
+//       bounds the drift between Q and R. The iteration runs in binary16
+//       (X0 = u/||u|| and every R, P, Q, X stay within its range; its 11-bit
+//       significand keeps R accurate); the result o is written in bf16.
 #include "b2o_common.cuh"
 #include "b2o_internal.h"
 
@@ -71,6 +73,31 @@ __global__ void norm_finalize_kernel(const float* __restrict__ partial, int npar
   }
 }
 
+// X0 = binary16(u * scale[s]): the normalised Gram-iteration input.
+__global__ void to_half_scaled_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
+                                      const float* __restrict__ scale) {
+  const int s = blockIdx.y;
+  const float sc = scale[s];
+  const uint16_t* u = U + static_cast<int64_t>(s) * rc;
+  uint16_t* x = X + static_cast<int64_t>(s) * rc;
+  const int64_t nvec = (rc % 8 == 0) ? rc / 8 : 0;  // 16-byte vectors only when every matrix is aligned
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint4 in = reinterpret_cast<const uint4*>(u)[v];
+    uint32_t w[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint16_t lo = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu)) * sc);
+      const uint16_t hi = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] >> 16)) * sc);
+      w[h] = lo | (static_cast<uint32_t>(hi) << 16);
+    }
+    reinterpret_cast<uint4*>(x)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (int64_t i = nvec * 8 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rc;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    x[i] = f32_to_f16(bf16_to_f32(u[i]) * sc);
+}
+
 // X0 = bf16(u / d[s]) (the division of zeropower_via_newtonschulz5, sol_modules.py:283).
 __global__ void ns_normalize_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
                                     const float* __restrict__ div) {
@@ -87,6 +114,7 @@ namespace {
 
 struct Batch {
   int S, r, c, m, n;
+  int half;   // 1: iterate in binary16 (Gram mode); 0: bfloat16 (quintic mode)
   bool tall;
   int64_t rc, mm;
   cudaStream_t st;
@@ -95,21 +123,21 @@ struct Batch {
 // Operand describing the stored (r, c) matrix X as op(X) with rows = m-side.
 // wide (r <= c): X itself; tall: X^T, read MN-major.
 Operand x_as_mk(const Batch& b, const uint16_t* X) {
-  return Operand{X, b.c, b.rc, b.tall ? 0 : 1};
+  return Operand{X, b.c, b.rc, b.tall ? 0 : 1, b.half};
 }
-Operand sq(const Batch& b, const uint16_t* Mx) { return Operand{Mx, b.m, b.mm, 1}; }
+Operand sq(const Batch& b, const uint16_t* Mx) { return Operand{Mx, b.m, b.mm, 1, b.half}; }
 
-Epilogue epi0(uint16_t* D, int64_t ldd, int64_t strideD, float alpha, const float* scale) {
+Epilogue epi0(uint16_t* D, int64_t ldd, int64_t strideD, float alpha, const float* scale, int d_half) {
   Epilogue e;
   memset(&e, 0, sizeof(e));
-  e.kind = 0; e.alpha = alpha; e.scale = scale; e.D = D; e.ldd = ldd; e.strideD = strideD;
+  e.kind = 0; e.alpha = alpha; e.scale = scale; e.D = D; e.ldd = ldd; e.strideD = strideD; e.d_half = d_half;
   return e;
 }
 
 // R = scale * X X^T (m x m, symmetric)
 int syrk(const Batch& b, const uint16_t* X, uint16_t* R, const float* scale) {
   const Operand A = x_as_mk(b, X);
-  return gemm(A, A, epi0(R, b.m, b.mm, 1.0f, scale), b.m, b.m, b.n, b.S, 1, b.st);
+  return gemm(A, A, epi0(R, b.m, b.mm, 1.0f, scale, b.half), b.m, b.m, b.n, b.S, 1, b.st);
 }
 
 // D (stored r x c) = L X in the m-side frame: wide D = L X, tall D = X L^T.
@@ -117,10 +145,10 @@ int apply_left(const Batch& b, const uint16_t* L, const uint16_t* X, Epilogue e)
   e.ldd = b.c; e.strideD = b.rc;
   if (!b.tall) {
     const Operand A = sq(b, L);
-    const Operand B{X, b.c, b.rc, 0};  // B[j][k] = X[k][j]
+    const Operand B{X, b.c, b.rc, 0, b.half};  // B[j][k] = X[k][j]
     return gemm(A, B, e, b.r, b.c, b.m, b.S, 0, b.st);
   }
-  const Operand A{X, b.c, b.rc, 1};
+  const Operand A{X, b.c, b.rc, 1, b.half};
   const Operand B = sq(b, L);          // B[j][k] = L[j][k]
   return gemm(A, B, e, b.r, b.c, b.m, b.S, 0, b.st);
 }
@@ -148,6 +176,7 @@ int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, 
 
   Batch b;
   b.S = S; b.r = r; b.c = c; b.m = std::min(r, c); b.n = std::max(r, c); b.tall = r > c;
+  b.half = mode == 1 ? 1 : 0;
   b.rc = static_cast<int64_t>(r) * c; b.mm = static_cast<int64_t>(b.m) * b.m; b.st = stream;
   uint8_t* base = static_cast<uint8_t*>(ws);
   auto pool = [&](int i) { return reinterpret_cast<uint16_t*>(base + L.pool_off + i * L.pool_stride); };
@@ -202,26 +231,33 @@ int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, 
   };
   auto release = [&](int i) { if (i >= 0) used[i] = false; };
 
+  // normalised binary16 copy of the front output (the Gram iteration runs in
+  // binary16: R, P and Q are bounded, and its 11-bit significand keeps the
+  // Gram matrix far more accurate than bfloat16 at the same tensor-core rate)
+  {
+    const int gx = static_cast<int>(std::min<int64_t>((rc / 8 + 255) / 256 + 1, std::max(1, num_sms() * 8 / S)));
+    to_half_scaled_kernel<<<dim3(gx, S), 256, 0, stream>>>(U, Xa, rc, scal);
+    count_launch();
+    if (int e = check_launch("to_half_scaled")) return e;
+  }
   int R = alloc();
-  if ((rc_ = syrk(b, U, pool(R), scal + S))) return rc_;
-  const uint16_t* Xcur = U;
-  const float* pend = scal;   // the front output is scaled lazily by s
+  if ((rc_ = syrk(b, Xa, pool(R), nullptr))) return rc_;
+  const uint16_t* Xcur = Xa;
   int Q = -1;
   for (int t = 0; t < T; ++t) {
     const float a = coeffs[3 * t], bb = coeffs[3 * t + 1], cc = coeffs[3 * t + 2];
     if (is_reset(t)) {
       uint16_t* Xn = (Xcur == Xa) ? Xb : Xa;
-      if ((rc_ = apply_left(b, pool(Q), Xcur, epi0(Xn, 0, 0, 1.0f, pend)))) return rc_;
+      if ((rc_ = apply_left(b, pool(Q), Xcur, epi0(Xn, 0, 0, 1.0f, nullptr, 1)))) return rc_;
       release(Q); Q = -1;
       release(R); R = alloc();
       if ((rc_ = syrk(b, Xn, pool(R), nullptr))) return rc_;
       Xcur = Xn;
-      pend = nullptr;
     }
     const int P = alloc();
     Epilogue ep;
     memset(&ep, 0, sizeof(ep));
-    ep.kind = 1; ep.alpha = a; ep.beta = bb; ep.gamma = cc;
+    ep.kind = 1; ep.alpha = a; ep.beta = bb; ep.gamma = cc; ep.d_half = 1;
     ep.C = pool(R); ep.ldc = b.m; ep.strideC = b.mm; ep.D = pool(P);
     if ((rc_ = prod(b, pool(R), pool(R), ep, 1))) return rc_;
     bool p_owned_by_q = false;
@@ -229,21 +265,21 @@ int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, 
       Q = P; p_owned_by_q = true;
     } else {
       const int Qn = alloc();
-      if ((rc_ = prod(b, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr), 0))) return rc_;
+      if ((rc_ = prod(b, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
       release(Q); Q = Qn;
     }
     const bool need_r = (t < T - 1) && !is_reset(t + 1);
     if (need_r) {
       const int T1 = alloc();
-      if ((rc_ = prod(b, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr), 0))) return rc_;
+      if ((rc_ = prod(b, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
       const int Rn = alloc();
-      if ((rc_ = prod(b, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr), 1))) return rc_;
+      if ((rc_ = prod(b, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
       release(T1); release(R); R = Rn;
     }
     if (!p_owned_by_q) release(P);
     if (R < 0 || Q < 0) { set_error("orthogonalize: workspace pool exhausted"); return -1; }
   }
-  Epilogue ef = epi0(out, 0, 0, 1.0f, pend);
+  Epilogue ef = epi0(out, 0, 0, 1.0f, nullptr, 0);  // o in bfloat16, as the reference returns it
   ef.rowsq = rowsq;
   return apply_left(b, pool(Q), Xcur, ef);
 }

@@ -16,6 +16,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libb2o.so"
 
 F32 = 0
 BF16 = 1
+F16 = 2
 
 c_void_p = C.c_void_p
 c_int = C.c_int
@@ -77,6 +78,9 @@ SIGNATURES = {
     "b2o_gemm_bf16": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int, c_void_p,
                               c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                               c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
+    "b2o_gemm": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int, c_void_p,
+                         c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
+                         c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
     "b2o_gemm_bf16_simt": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
                                    c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),

@@ -41,6 +41,7 @@ class EmaWeights:
         self._armed = False
         self._folded = set()
         self._attached = []
+        self._skip = set()  # indices another rank updates in a sharded step (see sharding.py)
 
     @property
     def weight(self) -> float:
@@ -93,11 +94,11 @@ class EmaWeights:
     @torch.no_grad()
     def update(self):
         if not self._armed:
-            self._standalone(list(range(len(self.params))))
+            self._standalone([i for i in range(len(self.params)) if i not in self._skip])
             if self.fuse:
                 self._arm()
             return
-        todo = [i for i in range(len(self.params)) if i not in self._folded]
+        todo = [i for i in range(len(self.params)) if i not in self._folded and i not in self._skip]
         self._folded.clear()
         self._standalone(todo)
 

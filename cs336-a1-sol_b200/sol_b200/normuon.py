@@ -41,7 +41,7 @@ class NorMuonGNS(torch.optim.Optimizer):
 
     def __init__(self, params, lr=2e-3, momentum=0.95, beta2=0.95, nesterov=True, ns_steps=5,
                  weight_decay=0.0, cautious_wd=False, bf16_master=False, *, orthogonalizer="gram",
-                 coefficients="polar_express", reset_iterations=(2,), norm_eps=1e-7, norm_safety=None):
+                 coefficients="polar_express", reset_iterations=(2,), norm_eps=1e-7, norm_safety=1.0):
         super().__init__(params, dict(lr=lr, momentum=momentum, beta2=beta2, nesterov=nesterov,
                                       ns_steps=ns_steps, weight_decay=weight_decay))
         if orthogonalizer not in ("gram", "quintic"):
@@ -52,14 +52,13 @@ class NorMuonGNS(torch.optim.Optimizer):
         self.coefficients = "quintic" if orthogonalizer == "quintic" else coefficients
         self.reset_iterations = tuple(int(x) for x in reset_iterations)
         self.norm_eps = float(norm_eps)
-        if norm_safety is None:
-            norm_safety = 1.01 if self.coefficients == "polar_express" else 1.0
         self.norm_safety = float(norm_safety)
         self._ws = {}
         self._tables = {}
         self._owned = None         # set of id(param) this rank updates (sharded step), None = all
         self._ema = None           # EmaWeights folded into the apply pass (set when it arms)
         self._ema_weight = 0.0
+        self._timing_events = None  # list -> (start, end) CUDA events around each orthogonalisation
         register_optimizer(self)
 
     # ------------------------------------------------------------------ hooks
@@ -112,11 +111,19 @@ class NorMuonGNS(torch.optim.Optimizer):
         lib = _lib.load()
         coeffs, resets, nres = self._table(ns_steps)
         mode = 0 if self.orthogonalizer == "quintic" else 1
+        ev = self._timing_events
+        if ev is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
         rc = lib.b2o_orthogonalize(U.data_ptr(), partial.data_ptr(), S, r, c, mode, coeffs, ns_steps, resets,
                                    nres, self.norm_eps, self.norm_safety, ws["ortho"].data_ptr(),
                                    ws["ortho"].numel(), out.data_ptr(), ws["rowsq"].data_ptr(),
                                    _lib.stream_ptr(U.device))
         _lib.check(rc, "orthogonalize")
+        if ev is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            ev.append((e0, e1))
 
     def _hook_overridden(self):
         return ("_orthogonalize_batch" in self.__dict__ or

@@ -17,9 +17,16 @@
   3. The polynomial is rescaled so that it is centred on 1 over the true
      interval [l, u] (1 - p(l) = p(u) - 1), and the interval is mapped:
      l <- p(l), u <- p(u).
+  4. Safety margin: each polynomial is designed for [l, u * (1 + margin)], so a
+     singular value pushed slightly above the nominal top by rounding stays in
+     the region where the next polynomial is bounded. Without the margin the
+     composition diverges in 16-bit arithmetic for singular values that land at
+     the top of an interval (the equioscillation maximum is attained inside the
+     interval, so such values are common).
 
-  ``l0`` and ``cushion`` are this library's choices (documented defaults); the
-  table is therefore "parity unpinned" against the package's own constants.
+  ``l0``, ``cushion`` and ``margin`` are this library's choices (documented
+  defaults); the table is therefore "parity unpinned" against the package's
+  own constants.
 """
 from __future__ import annotations
 
@@ -92,17 +99,18 @@ def optimal_odd_quintic(lo: float, hi: float, iters: int = 100, tol: float = 1e-
     return coef[0], coef[1], coef[2], E
 
 
-def polar_express(steps: int = 5, l0: float = 1e-3, cushion: float = 0.02):
+def polar_express(steps: int = 5, l0: float = 1e-3, cushion: float = 0.02, margin: float = 0.05):
     """Per-step (a, b, c) table of length ``steps`` (float64 values)."""
     lo, hi = float(l0), 1.0
     table = []
     for _ in range(steps):
-        a, b, c, _ = optimal_odd_quintic(max(lo, cushion * hi), hi)
-        pl, pu = _poly((a, b, c), lo), _poly((a, b, c), hi)
+        top = hi * (1.0 + margin)
+        a, b, c, _ = optimal_odd_quintic(max(lo, cushion * top), top)
+        pl, pu = _poly((a, b, c), lo), _poly((a, b, c), top)
         k = 2.0 / (pl + pu)
         a, b, c = a * k, b * k, c * k
         table.append((a, b, c))
-        lo, hi = _poly((a, b, c), lo), _poly((a, b, c), hi)
+        lo, hi = _poly((a, b, c), lo), _poly((a, b, c), top)
     return table
 
 

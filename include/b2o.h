@@ -19,7 +19,7 @@
  *     CUDA launch/runtime error code.
  *   - Device-side failures (a bounded wait that ran out) set a device error word
  *     instead of trapping; b2o_check_device_error() reads and clears it.
- *   - dtype codes: B2O_F32 = 0, B2O_BF16 = 1.
+ *   - dtype codes: B2O_F32 = 0, B2O_BF16 = 1, B2O_F16 = 2 (IEEE binary16).
  */
 #ifndef B2O_H_
 #define B2O_H_
@@ -33,6 +33,7 @@ extern "C" {
 
 #define B2O_F32 0
 #define B2O_BF16 1
+#define B2O_F16 2
 
 /* Error/status plumbing (no reference counterpart: the reference raises Python
  * exceptions from torch; these carry the same information across the C ABI). */
@@ -166,6 +167,18 @@ int b2o_gemm_bf16(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajo
                   int M, int N, int K, int batch, int epi, int sym,
                   float alpha, float beta, float gamma, const float* d_scale,
                   float* d_rowsq, void* stream);
+
+/* General form: in_dtype (A, B and C) and out_dtype (D) are B2O_BF16 or
+ * B2O_F16; epilogues 2 and 3 need bf16 throughout. b2o_gemm_bf16 is this call
+ * with both dtypes bf16. No reference counterpart (the reference multiplies
+ * with torch.matmul / the gram-newton-schulz package). */
+int b2o_gemm(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor,
+             const uint16_t* d_B, int64_t ldb, int64_t strideB, int b_kmajor,
+             uint16_t* d_D, int64_t ldd, int64_t strideD,
+             const uint16_t* d_C, int64_t ldc, int64_t strideC,
+             int M, int N, int K, int batch, int in_dtype, int out_dtype, int epi, int sym,
+             float alpha, float beta, float gamma, const float* d_scale,
+             float* d_rowsq, void* stream);
 
 /* The same product on CUDA cores (no tensor cores, no mirroring); a test hook
  * that checks the tensor-core path against an independent kernel. No

@@ -14,20 +14,22 @@ against the package. It follows the schedule the engine runs:
       if t < T-1 and t+1 not a restart:  R = P R P
   out = Q X
 
-``bf16=True`` rounds every product to bf16 as the engine stores them;
-``bf16=False`` runs in float64 (the exact-arithmetic target).
+``store=torch.float16`` (or bfloat16) rounds X0 and every product to that type
+as the engine stores them (binary16 is what the engine's Gram mode uses);
+``store=None`` runs in float64 (the exact-arithmetic target).
 """
 from __future__ import annotations
 
 import torch
 
 
-def _rnd(x, bf16):
-    return x.to(torch.bfloat16).to(x.dtype) if bf16 else x
+def _rnd(x, store):
+    return x.to(store).to(x.dtype) if store is not None else x
 
 
-def gram_ns(U: torch.Tensor, table, resets=(2,), eps=1e-7, safety=1.0, bf16=False) -> torch.Tensor:
-    dt = torch.float32 if bf16 else torch.float64
+def gram_ns(U: torch.Tensor, table, resets=(2,), eps=1e-7, safety=1.0, store=None) -> torch.Tensor:
+    bf16 = store
+    dt = torch.float32 if store is not None else torch.float64
     outs = []
     T = len(table)
     for u in U:
@@ -35,9 +37,10 @@ def gram_ns(U: torch.Tensor, table, resets=(2,), eps=1e-7, safety=1.0, bf16=Fals
         tall = u.shape[0] > u.shape[1]
         X = u.t() if tall else u
         s = 1.0 / (torch.linalg.norm(u) * safety + eps)
-        R = _rnd(s * s * (X @ X.t()), bf16)
+        X = _rnd(X * s, bf16)
+        R = _rnd(X @ X.t(), bf16)
         Q = None
-        pend = s
+        pend = 1.0
         for t in range(T):
             a, b, c = (float(v) for v in table[t])
             if t > 0 and t in resets:
@@ -52,7 +55,8 @@ def gram_ns(U: torch.Tensor, table, resets=(2,), eps=1e-7, safety=1.0, bf16=Fals
             if t < T - 1 and not (t + 1 in resets):
                 T1 = _rnd(P @ R, bf16)
                 R = _rnd(T1 @ P, bf16)
-        out = _rnd(pend * (Q @ X), bf16)
+        out = pend * (Q @ X)
+        out = out.to(torch.bfloat16).to(dt) if store is not None else out
         outs.append(out.t() if tall else out)
     return torch.stack(outs)
 

@@ -117,12 +117,20 @@ def make_reference_adamw(groups, betas=(0.9, 0.95), eps=1e-8):
     return torch.optim.AdamW(groups, betas=betas, eps=eps, fused=True)
 
 
+def _fma32(a, b, c):
+    """fp32 fused multiply-add: a*b + c with one rounding (exact product in float64;
+    the float64 sum is then rounded once more to fp32, which matches a true fma
+    except in vanishingly rare double-rounding cases)."""
+    return (a.double() * b.double() + c.double()).float()
+
+
 class MasterAdamW:
     """AdamW with a bf16 low-mantissa remainder, fp32 moments and cautious decay.
 
     torch's fused AdamW element formula (ATen/native/cuda/fused_adam_utils.cuh,
-    ADAMW mode) applied to w = float(p) + float(rem), with NorMuon's cautious
-    mask and remainder split (sol_modules.py:406-424).
+    ADAMW mode: exp_avg = fma(b1, m, fma(-b1, g, g)), the same for exp_avg_sq)
+    applied to w = float(p) + float(rem), with NorMuon's cautious mask and
+    remainder split (sol_modules.py:406-424).
     """
 
     def __init__(self, params, lr, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, cautious=False):
@@ -134,32 +142,32 @@ class MasterAdamW:
 
     @torch.no_grad()
     def step(self):
-        b1, b2 = (torch.tensor(x, dtype=torch.float32) for x in self.betas)
-        lr = torch.tensor(self.lr, dtype=torch.float32)
-        wd = torch.tensor(self.wd, dtype=torch.float32)
-        eps = torch.tensor(self.eps, dtype=torch.float32)
+        f32 = lambda x: torch.tensor(x, dtype=torch.float32)  # noqa: E731
+        b1, b2 = f32(self.betas[0]), f32(self.betas[1])
+        lr, wd, eps = f32(self.lr), f32(self.wd), f32(self.eps)
         for p, st in zip(self.params, self.state):
             if p.grad is None:
                 continue
             st["step"] += 1
-            t = torch.tensor(float(st["step"]), dtype=torch.float32)
+            t = f32(float(st["step"]))
             bc1 = 1 - torch.pow(b1, t)
             bc2_sqrt = torch.sqrt(1 - torch.pow(b2, t))
             g = p.grad.float()
             w = p.float()
             if st["rem"] is not None:
                 w = w + st["rem"].float()
-            m = b1 * st["m"] + (g - b1 * g)
-            v = b2 * st["v"] + (g * g - b2 * (g * g))
+            m = _fma32(b1, st["m"], _fma32(-b1, g, g))
+            g2 = g * g
+            v = _fma32(b2, st["v"], _fma32(-b2, g2, g2))
             if self.wd:
                 lr_wd = lr * wd
                 if self.cautious:
                     mask = ((m * w) > 0).float()
                     w = w * (1 - lr_wd * mask)
                 else:
-                    w = w - lr_wd * w
+                    w = _fma32(-lr_wd, w, w)
             denom = torch.sqrt(v) / bc2_sqrt + eps
-            w = w - (lr / bc1 * m) / denom
+            w = w - ((lr / bc1) * m) / denom
             st["m"], st["v"] = m, v
             if st["rem"] is not None:
                 pn = w.to(torch.bfloat16)

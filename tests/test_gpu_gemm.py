@@ -114,3 +114,21 @@ def test_large_k_tall_syrk(cuda):
     torch.cuda.synchronize()
     ref = X.float().transpose(1, 2) @ X.float()
     torch.testing.assert_close(D.float(), ref.to(torch.bfloat16).float(), rtol=1e-2, atol=1e-2 * ref.abs().max().item())
+
+
+@pytest.mark.parametrize("out_dtype", [2, 1])
+def test_binary16_operands(cuda, out_dtype):
+    """kind::f16 with binary16 operands (the Gram iteration's storage type)."""
+    gen = torch.Generator(device=cuda).manual_seed(21)
+    M, N, K, batch = 384, 512, 320, 2
+    A = torch.randn(batch, M, K, generator=gen, device=cuda).half()
+    X = torch.randn(batch, K, N, generator=gen, device=cuda).half()   # B MN-major
+    odt = torch.float16 if out_dtype == 2 else torch.bfloat16
+    D = torch.empty(batch, M, N, device=cuda, dtype=odt)
+    lib = _lib.load()
+    rc = lib.b2o_gemm(A.data_ptr(), K, M * K, 1, X.data_ptr(), N, K * N, 0, D.data_ptr(), N, M * N, None, 0, 0,
+                      M, N, K, batch, 2, out_dtype, 0, 0, 1.0, 0.0, 0.0, None, None, _lib.stream_ptr())
+    _lib.check(rc, "gemm f16")
+    torch.cuda.synchronize()
+    ref = A.float() @ X.float()
+    torch.testing.assert_close(D.float(), ref.to(odt).float(), rtol=1e-2, atol=1e-2 * ref.abs().max().item())

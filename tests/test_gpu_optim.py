@@ -5,9 +5,13 @@ Tolerances (stated where they are checked):
   * AdamW / EMA element math: fp32 values within 2 ulp; bf16 values equal or
     one bf16 ulp apart where the fp32 result sits on a rounding boundary.
   * bf16 mantissa split / recombine: bit-exact given the same fp32 weight.
-  * Orthogonalised NorMuon updates: relative Frobenius error <= 1e-2 on the
-    cumulative update after 10 steps (bf16 Newton-Schulz is itself sensitive at
-    the 1e-2 level to GEMM accumulation order).
+  * Orthogonalised NorMuon updates: relative Frobenius error of the cumulative
+    update after 10 steps <= 1e-2 for fp32 parameters. The reference's
+    orthogonaliser is bf16 Newton-Schulz; changing only the order of fp32
+    accumulation inside its GEMMs moves its output by ~0.5-1.3 % (measured on
+    the CPU by tests/test_host_cpu.py::test_bf16_newton_schulz_noise_floor), so
+    for bf16 parameters the bound is 1.5e-2 with mantissa tracking and 2.5e-2
+    without it (there every step also rounds the weight itself to bf16).
 """
 import math
 
@@ -104,7 +108,14 @@ def test_adamw_master_mode_vs_oracle(cuda):
         assert_f32_ulps(so["exp_avg_sq"], st["v"], what="exp_avg_sq")
         w_ours = a.data.float().cpu() + so["mant_rem"].float().cpu()
         w_orc = b.data.float() + st["rem"].float()
-        assert_f32_ulps(w_ours, w_orc, ulps=2, what="reconstructed fp32 weight")
+        # bf16 parameter + bf16 remainder resolves |w| to about 2^-16 |w| (16
+        # significant bits). The bias corrections use powf on the GPU and
+        # torch.pow on the CPU (an ulp apart at most); such one-ulp differences
+        # of the fp32 weight can move the remainder's own bf16 rounding by one
+        # step, so the pair agrees to two remainder steps.
+        tol = 2.0 ** -15 * w_orc.abs() + 4 * _ulp_f32(w_orc)
+        assert ((w_ours - w_orc).abs() <= tol).all(), "reconstructed weight"
+        assert_bf16_close(a.data, b.data, "bf16 parameter", min_exact=0.999)
 
 
 def test_mantissa_split_is_bit_exact(cuda):
@@ -159,15 +170,15 @@ def _normuon_pair(cfg, steps, cautious, bf16_master, orthogonalizer, coefficient
     return names, muon_c, muon_g, p0, orc, eng
 
 
-@pytest.mark.parametrize("cfg,cautious,mt", [(synth.C1, False, False), (synth.MICRO, True, True),
-                                              (synth.MICRO, False, False)])
-def test_normuon_quintic_matches_reference(cuda, cfg, cautious, mt):
+@pytest.mark.parametrize("cfg,cautious,mt,bound", [(synth.C1, False, False, 1e-2), (synth.MICRO, True, True, 1.5e-2),
+                                                    (synth.MICRO, False, False, 2.5e-2)])
+def test_normuon_quintic_matches_reference(cuda, cfg, cautious, mt, bound):
     names, pc, pg, p0, orc, eng = _normuon_pair(cfg, 10, cautious, mt, "quintic")
     du_c = torch.cat([(p.detach().float() - a).reshape(-1) for p, a in zip(pc, p0)])
     du_g = torch.cat([(p.detach().float().cpu() - a).reshape(-1) for p, a in zip(pg, p0)])
     err = rel_fro(du_g, du_c)
     print(f"{cfg.name}: cumulative update rel. Frobenius error after 10 steps = {err:.2e}")
-    assert err <= 1e-2
+    assert err <= bound
     for i, (a, b) in enumerate(zip(pc, pg)):
         e = rel_fro(b.detach().float().cpu() - p0[i], a.detach().float() - p0[i])
         assert e <= 3e-2, f"{names[i]}: per-matrix update error {e:.3e}"
@@ -181,13 +192,31 @@ def test_normuon_quintic_matches_reference(cuda, cfg, cautious, mt):
 
 
 def test_normuon_gram_quintic_table_matches_reference(cuda):
-    """Gram Newton-Schulz with the quintic table equals standard NS in exact arithmetic."""
+    """Gram Newton-Schulz with the quintic table equals standard NS in exact
+    arithmetic; the engine runs it in binary16, the reference in bf16."""
     names, pc, pg, p0, orc, eng = _normuon_pair(synth.MICRO, 10, True, True, "gram", "quintic")
     du_c = torch.cat([(p.detach().float() - a).reshape(-1) for p, a in zip(pc, p0)])
     du_g = torch.cat([(p.detach().float().cpu() - a).reshape(-1) for p, a in zip(pg, p0)])
     err = rel_fro(du_g, du_c)
     print(f"gram/quintic: cumulative update rel. Frobenius error after 10 steps = {err:.2e}")
-    assert err <= 1e-2
+    assert err <= 2.5e-2
+
+
+@pytest.mark.parametrize("r,c", [(384, 128), (128, 384), (512, 512), (3072, 1024)])
+def test_gram_binary16_is_closer_to_exact_than_reference(cuda, r, c):
+    """On one orthogonalisation, the engine's binary16 Gram iteration (quintic
+    table) is nearer to exact-arithmetic Newton-Schulz than the reference's own
+    bf16 iteration is."""
+    g = torch.Generator().manual_seed(r * 3 + c)
+    U = (torch.randn(2, r, c, generator=g) * 1e-3).to(torch.bfloat16)
+    opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=cuda))], orthogonalizer="gram",
+                     coefficients="quintic")
+    out = opt._orthogonalize_batch(U.cuda(), 5).float().cpu()
+    exact = gram_ns_ref.gram_ns(U, [polar_express.QUINTIC] * 5)
+    ref_bf16 = ref_step.ortho_batch_quintic(U, 5).float()
+    e_eng, e_ref = rel_fro(out, exact), rel_fro(ref_bf16, exact)
+    print(f"({r},{c}) vs exact NS: engine gram/binary16 {e_eng:.2e}, reference bf16 {e_ref:.2e}")
+    assert e_eng < 1e-2 and e_eng < e_ref
 
 
 @pytest.mark.parametrize("r,c", [(256, 256), (768, 256), (256, 1408), (1024, 1024), (8, 128)])
@@ -198,26 +227,30 @@ def test_gram_polar_express_vs_fp64_restatement(cuda, r, c):
                      coefficients="polar_express")
     out = opt._orthogonalize_batch(U.cuda(), 5)
     torch.cuda.synchronize()
-    ref64 = gram_ns_ref.gram_ns(U, polar_express.polar_express(5), safety=opt.norm_safety)
-    err = rel_fro(out.float(), ref64)
-    print(f"({r},{c}) gram/PE vs fp64: {err:.3e}")
-    assert err < 0.12
+    table = polar_express.polar_express(5)
+    ref64 = gram_ns_ref.gram_ns(U, table, safety=opt.norm_safety)
+    emu16 = gram_ns_ref.gram_ns(U, table, safety=opt.norm_safety, store=torch.float16)
+    err, err_emu = rel_fro(out.float(), ref64), rel_fro(emu16, ref64)
+    print(f"({r},{c}) gram/PE binary16 engine vs fp64: {err:.3e} (CPU binary16 emulation: {err_emu:.3e})")
+    assert err < max(3e-2, 2.5 * err_emu)
     pf = gram_ns_ref.polar_factor(U)
     assert rel_fro(out.float(), pf) < 0.25
 
 
 # -------------------------------------------------------------- full step --
 def test_full_step_with_ema_matches_reference(cuda):
-    """build_optimizers + EmaWeights (folded into the passes) vs the oracle's
-    muon -> adamw -> ema step on the MICRO recipe set, 6 steps."""
+    """build_optimizers + EmaWeights (EMA folded into the passes) vs the reference
+    step muon -> adamw -> ema (oracle/ref_step.RefStep, bit-exact with the
+    reference on the CPU) run with torch on the same GPU: torch's CUDA fused
+    AdamW and bf16 cuBLAS Newton-Schulz, 6 steps of the MICRO recipe set."""
     cfg = synth.MICRO
     kw = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
-    mc = synth.SyntheticLM(cfg, seed=0)
+    mr = synth.SyntheticLM(cfg, seed=0).cuda()
     mg = synth.SyntheticLM(cfg, seed=0).cuda()
-    ref = ref_step.RefStep(mc, **kw)
+    ref = ref_step.RefStep(mr, **kw)
     muon, adamw = build_optimizers(mg, orthogonalizer="quintic", **kw)
     ema = EmaWeights(mg, 0.999)
-    p0 = [p.detach().clone().float() for p in mc.parameters()]
+    p0 = [p.detach().clone().float() for p in mr.parameters()]
     for it in range(6):
         frac = (it + 1) / 5
         ref.muon.group["lr"] = ref.muon.group["base_lr"] * frac
@@ -226,31 +259,36 @@ def test_full_step_with_ema_matches_reference(cuda):
         for opt in (muon, adamw):
             for gg in opt.param_groups:
                 gg["lr"] = gg["base_lr"] * frac
-        grads = synth.make_grads(mc, it, seed=0)
-        synth.set_grads(mc, grads)
-        synth.set_grads(mg, [x.cuda() for x in grads])
+        grads = synth.make_grads(mr, it, seed=0)
+        synth.set_grads(mr, grads)
+        synth.set_grads(mg, [x.clone() for x in grads])
         ref.step()
         muon.step()
         adamw.step()
         ema.update()
     torch.cuda.synchronize()
     assert ema._armed and ema._folded == set()
-    named_c = list(mc.named_parameters())
+    named_r = list(mr.named_parameters())
     named_g = dict(mg.named_parameters())
-    muon_names = set(ref_step.route(named_c)[0])
-    for i, (n, pcpu) in enumerate(named_c):
+    muon_names = set(ref_step.route(named_r)[0])
+    num = den = 0.0
+    for i, (n, pr) in enumerate(named_r):
         pgpu = named_g[n]
         if n in muon_names:
-            e = rel_fro(pgpu.detach().float().cpu() - p0[i], pcpu.detach().float() - p0[i])
-            assert e < 3e-2, f"{n}: {e}"
+            du_g, du_r = pgpu.detach().float() - p0[i], pr.detach().float() - p0[i]
+            num += float((du_g - du_r).pow(2).sum())
+            den += float(du_r.pow(2).sum())
+            assert rel_fro(ema.shadow[i] - p0[i], ref.shadow[i] - p0[i]) < 3e-2
         else:
-            assert_bf16_close(pgpu.data, pcpu.data, n, min_exact=0.995)
-            ms, mo = adamw.state[pgpu], ref.adamw.state[pcpu]
-            assert_bf16_close(ms["exp_avg"], mo["exp_avg"], n + "/exp_avg", min_exact=0.995)
-        # EMA: lerp of each step's params; differences only through the params themselves
-        sh_g = ema.shadow[i].cpu()
-        sh_c = ref.shadow[i]
-        assert rel_fro(sh_g - p0[i], sh_c - p0[i]) < 3e-2 or torch.equal(sh_g, sh_c)
+            # AdamW: torch's CUDA fused formula, reproduced bit for bit
+            assert torch.equal(pgpu.data, pr.data), n
+            ms, mo = adamw.state[pgpu], ref.adamw.state[pr]
+            assert torch.equal(ms["exp_avg"], mo["exp_avg"]) and torch.equal(ms["exp_avg_sq"], mo["exp_avg_sq"]), n
+            # EMA of identical parameters: torch's lerp formula in fp32
+            assert_f32_ulps(ema.shadow[i], ref.shadow[i], ulps=2, what=f"ema {n}")
+    err = (num / den) ** 0.5
+    print(f"full step: NorMuon cumulative update rel. Frobenius error after 6 steps = {err:.2e}")
+    assert err < 1.5e-2
 
 
 def test_ema_folded_equals_standalone(cuda):

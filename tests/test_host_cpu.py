@@ -49,13 +49,48 @@ def test_polar_express_table_properties():
     assert 0.8 < min(ys) and max(ys) < 1.2
     # ... much tighter than the quintic constant iteration
     yq = [polar_express.apply_table([polar_express.QUINTIC] * 5, x) for x in xs]
-    assert (max(ys) - min(ys)) < 0.5 * (max(yq) - min(yq))
-    # each step is centred on 1 over its interval (recentred minimax)
+    assert (max(ys) - min(ys)) < 0.75 * (max(yq) - min(yq))
+    # each step is centred on 1 over its (margin-widened) interval
     lo, hi = 1e-3, 1.0
     for coef in table:
-        pl, pu = polar_express._poly(coef, lo), polar_express._poly(coef, hi)
+        top = hi * 1.05
+        pl, pu = polar_express._poly(coef, lo), polar_express._poly(coef, top)
         assert abs((pl + pu) / 2 - 1) < 1e-12
         lo, hi = pl, pu
+
+
+def _scalar_gram(sig, table, store, resets=(2,)):
+    """The Gram schedule on 1x1 matrices (one singular value), every product stored in `store`."""
+    def rnd(v):
+        return v.to(store).double() if store is not None else v
+    X0 = rnd(sig)
+    R, Q, X = rnd(X0 * X0), None, X0
+    T = len(table)
+    for t, (a, b, c) in enumerate(table):
+        if t > 0 and t in resets:
+            X = rnd(Q * X)
+            R = rnd(X * X)
+            Q = None
+        P = rnd(a + b * R + c * rnd(R * R))
+        Q = P if Q is None else rnd(Q * P)
+        if t < T - 1 and (t + 1) not in resets:
+            R = rnd(rnd(P * R) * P)
+    return rnd(Q * X)
+
+
+def test_polar_express_table_is_stable_in_binary16():
+    """Across singular values in [2e-3, 1] the binary16 Gram iteration stays within a
+    few percent of the exact composition (no divergence at interval tops)."""
+    sig = torch.logspace(-2.7, 0, 4000, dtype=torch.float64)
+    table = polar_express.polar_express(5)
+    exact = _scalar_gram(sig, table, None)
+    half = _scalar_gram(sig, table, torch.float16)
+    err = ((half - exact).abs() / exact.abs())
+    assert err.max() < 0.08 and err.quantile(0.99) < 0.03
+    # without the safety margin the same procedure diverges somewhere
+    bad = polar_express.polar_express(5, margin=0.0)
+    e2 = ((_scalar_gram(sig, bad, torch.float16) - _scalar_gram(sig, bad, None)).abs() / _scalar_gram(sig, bad, None).abs())
+    assert e2.max() > 1.0
 
 
 def test_remez_equioscillation():
@@ -161,3 +196,35 @@ def test_normuon_param_group_keys_match_reference():
 def test_ctypes_structs_match_header_layout():
     assert ctypes.sizeof(_lib.AdamwTensor) == 6 * 8 + 8 + 4 + 4
     assert ctypes.sizeof(_lib.AdamwGroup) == 8 * 4
+
+
+def test_bf16_newton_schulz_noise_floor():
+    """The reference's bf16 quintic Newton-Schulz (run on the CPU, bit-exact with
+    transformer_lm.sol_modules) against the same iteration with every GEMM
+    accumulated in float64 before the identical bf16 rounding: only the
+    accumulation order differs, yet the outputs move by several 1e-3 relative
+    Frobenius. This is the floor for comparing two bf16 implementations."""
+    a, b, c = ref_step.QUINTIC
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+
+    def ns_f64_acc(G):
+        X = G.bfloat16()
+        X = X / (X.norm() + 1e-7)
+        tr = G.size(0) > G.size(1)
+        if tr:
+            X = X.t()
+        mm = lambda x, y: bf(x.double() @ y.double())  # noqa: E731
+        for _ in range(5):
+            A = mm(X, X.t())
+            B = bf(bf(b * A.float()) + bf(c * mm(A, A).float()))
+            X = bf(bf(a * X.float()) + mm(B, X).float())
+        return X.t() if tr else X
+
+    g = torch.Generator().manual_seed(0)
+    errs = []
+    for shape in [(384, 128), (128, 384), (256, 256), (768, 256)]:
+        G = torch.randn(shape, generator=g) * 1e-3
+        ref = ref_step.zeropower_ns5(G).double()
+        alt = ns_f64_acc(G).double()
+        errs.append((torch.linalg.norm(ref - alt) / torch.linalg.norm(ref)).item())
+    assert max(errs) > 3e-3, errs
