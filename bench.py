@@ -373,6 +373,93 @@ def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, 
             "d2h_bytes_per_step": out.numel() * out.element_size()}
 
 
+# ----------------------------------------------------------- micro legs ---
+def micro_gram(args, dev):
+    """batched orthogonalisation, 14 matrices per shape,
+    5 iterations, N(0,1) inputs scaled to unit spectral norm."""
+    from sol_b200 import NorMuonGNS
+    shapes = [tuple(int(x) for x in s.split("x")) for s in args.shape.split(",")]
+    peak_tf, _, peak_kind = peaks()
+    out = []
+    for (r, c) in shapes:
+        g = torch.Generator(device=dev).manual_seed(0)
+        U = torch.randn(14, r, c, generator=g, device=dev)
+        U = U / torch.linalg.matrix_norm(U, ord=2, keepdim=True)
+        U = U.to(torch.bfloat16)
+        opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=dev))], orthogonalizer=args.orthogonalizer,
+                         coefficients=args.coefficients)
+        o = torch.empty_like(U)
+        ws = opt._workspace(dev, 14, r, c)
+        part = ws["partial"].view(14, -1)
+        part.zero_()
+        part[:, 0] = U.float().pow(2).sum(dim=(1, 2))
+        for _ in range(args.warmup):
+            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1) / args.steps
+        mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
+        fl = 14 * gram_flops(min(r, c), max(r, c), mode=mode)
+        tf = fl / (ms * 1e-3) / 1e12
+        out.append({"shape": f"14x{r}x{c}", "ms": ms, "tflops": tf, "frac": tf / peak_tf})
+    return {"metric": "Gram-NS TFLOP/s", "value": statistics.mean(x["tflops"] for x in out), "unit": "TFLOP/s",
+            "higher_is_better": True, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16/f16",
+            "data": "synthetic", "config": {"workload": "configs[2] Gram-NS microbenchmark",
+                                             "orthogonalizer": args.orthogonalizer, "coefficients": args.coefficients},
+            "per_shape": out, "peak": peak_tf, "peak_kind": f"{peak_kind} bf16 burst"}
+
+
+def micro_adamw(args, dev):
+    """streaming AdamW+EMA over 7 x 32768 x 1024 + 1M scalars,
+    bf16 params + bf16 remainder, fp32 moments, fp32 EMA, cautious decay 0.1, step 100."""
+    from sol_b200 import AdamW, EmaWeights
+    g = torch.Generator(device=dev).manual_seed(0)
+    params = [torch.nn.Parameter((torch.randn(32768, 1024, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+              for _ in range(7)]
+    params.append(torch.nn.Parameter(torch.ones(1 << 20, device=dev, dtype=torch.bfloat16)))
+    for p in params:
+        p.grad = (torch.randn(p.shape, generator=g, device=dev) * 1e-4).to(torch.bfloat16)
+    opt = AdamW(params, lr=2.4e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, master="bf16_mt",
+                cautious_wd=True)
+    holder = torch.nn.Module()
+    for i, p in enumerate(params):
+        holder.register_parameter(f"t{i}", p)
+    ema = EmaWeights(holder, 0.999)
+    for p in params:
+        opt._init_state(p)
+        opt._steps[id(p)] = 99
+    ema.update()  # arms folding
+    for _ in range(args.warmup):
+        opt.step()
+        ema.update()
+    torch.cuda.synchronize()
+    s0 = torch.cuda.Event(enable_timing=True)
+    s1 = torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(args.steps):
+        opt.step()
+        ema.update()
+    s1.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / args.steps
+    n = sum(p.numel() for p in params)
+    gbs = n * 34 / (ms * 1e-3) / 1e9
+    _, peak_gbs, peak_kind = peaks()
+    return {"metric": "AdamW+EMA GB/s", "value": gbs, "unit": "GB/s", "higher_is_better": True, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "dtype": "bf16+fp32", "data": "synthetic",
+            "config": {"workload": "configs[3] streaming AdamW+EMA", "elements": n,
+                       "bytes_per_element": 34, "ema": "fp32 (bf16 shadow underflows at decay 0.999)"},
+            "ms_per_step": ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s", "frac": gbs / peak_gbs,
+                         "traffic": None, "peak_kind": f"{peak_kind} copy"}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,6 +473,9 @@ def main():
     ap.add_argument("--coefficients", default="polar_express", choices=["polar_express", "quintic"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", choices=["gram", "adamw"], default=None,
+                    help="run a BASELINE micro-benchmark (configs[2] / configs[3]) instead of the full step")
+    ap.add_argument("--shape", default="1024x1024,3072x1024,5632x1024,1024x5632")
     args = ap.parse_args()
     if args.device is None:
         args.device = "cuda" if args.impl == "engine" else "cpu"
@@ -397,6 +487,13 @@ def main():
             print(json.dumps(reference_arm(args, world, rank)), flush=True)
         return
     world, rank, local = dist_setup(args)
+    if args.micro:
+        dev = torch.device("cuda", local)
+        _lib.load()
+        line = micro_gram(args, dev) if args.micro == "gram" else micro_adamw(args, dev)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return
     try:
         if args.impl == "reference":
             line = reference_arm(args, world, rank)

@@ -54,7 +54,18 @@ int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int 
 bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K);
 
 // ---- ortho.cu
+struct OrthoGroup {
+  const uint16_t* U;       // front output (S, r, c) bf16
+  const float* partial;    // front sum-of-squares partials
+  uint16_t* out;           // o (S, r, c) bf16
+  float* rowsq;            // per-row partial sums of o^2
+  int S, r, c;
+};
 int64_t ortho_workspace_bytes(int S, int r, int c);
+int64_t ortho_workspace_bytes_multi(const OrthoGroup* g, int ng);
+int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float* coeffs, int T, const int* resets,
+                        int nresets, float norm_eps, float norm_safety, void* ws, int64_t ws_bytes,
+                        cudaStream_t stream);
 int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode,
                   const float* coeffs, int T, const int* resets, int nresets, float norm_eps,
                   float norm_safety, void* ws, int64_t ws_bytes, uint16_t* out, float* rowsq,

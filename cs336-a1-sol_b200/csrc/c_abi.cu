@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 namespace b2o {
 
@@ -126,6 +127,27 @@ int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r,
                       void* d_ws, int64_t ws_bytes, uint16_t* d_out, float* d_rowsq, void* stream) {
   return orthogonalize(d_u, d_partial, S, r, c, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, d_ws,
                        ws_bytes, d_out, d_rowsq, static_cast<cudaStream_t>(stream));
+}
+
+static std::vector<OrthoGroup> to_groups(const b2o_ortho_group* g, int ng) {
+  std::vector<OrthoGroup> v;
+  for (int i = 0; i < ng; ++i) v.push_back(OrthoGroup{g[i].u, g[i].partial, g[i].out, g[i].rowsq, g[i].S, g[i].r, g[i].c});
+  return v;
+}
+
+int64_t b2o_ortho_workspace_bytes_multi(const b2o_ortho_group* groups, int ngroups) {
+  if (!groups || ngroups <= 0) return -1;
+  auto v = to_groups(groups, ngroups);
+  return ortho_workspace_bytes_multi(v.data(), ngroups);
+}
+
+int b2o_orthogonalize_multi(const b2o_ortho_group* groups, int ngroups, int mode, const float* coeffs, int T,
+                            const int* resets, int nresets, float norm_eps, float norm_safety, void* d_ws,
+                            int64_t ws_bytes, void* stream) {
+  if (!groups || ngroups <= 0) { set_error("orthogonalize: no groups"); return -1; }
+  auto v = to_groups(groups, ngroups);
+  return orthogonalize_multi(v.data(), ngroups, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, d_ws,
+                             ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int64_t b2o_normuon_apply_scratch_floats(int S, int r) {

@@ -34,7 +34,11 @@ constexpr int B_BYTES = BN * BK * 2;            // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 columns
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Epilogue staging: per epilogue warp two 32x32 16-bit tiles (direct and
+// mirrored), 64-byte rows in the TMA 64-byte swizzle, written by TMA stores.
+constexpr int EPI_TILE_BYTES = 32 * 32 * 2;
+constexpr int EPI_BYTES = 4 * 2 * EPI_TILE_BYTES;  // 16 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct Params {
@@ -96,6 +100,28 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Byte offset of 16-bit element (row, col) in a 32x32 staging tile stored with
+// 64-byte rows under the TMA 64-byte swizzle (16-byte chunk index XOR bits 1-2 of the row).
+__device__ __forceinline__ uint32_t stage_off(int row, int col) {
+  const uint32_t chunk = static_cast<uint32_t>(col >> 3) ^ ((static_cast<uint32_t>(row) >> 1) & 3u);
+  return static_cast<uint32_t>(row) * 64u + (chunk << 4) + (static_cast<uint32_t>(col & 7) << 1);
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 __device__ __forceinline__ void fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -204,10 +230,11 @@ __device__ __forceinline__ float epi_value(const Params& p, int kind, float acc,
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ Params p) {
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -330,13 +357,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // --------------------------------------------------------- epilogue ---
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
+    // Each warp owns TMEM lanes [32*quad, 32*quad+32), i.e. 32 output rows, and
+    // moves them out 32 columns at a time: tcgen05.ld -> epilogue arithmetic in
+    // registers -> swizzled staging tile in shared memory -> TMA store (which
+    // clips rows/columns outside the matrix). Symmetric outputs skip chunks
+    // below the diagonal, store chunks above it twice (direct and mirrored)
+    // and symmetrise the diagonal chunk in shared memory before one store.
+    const int quad = warp & 3;
+    const uint32_t st_direct = smem_u32(epi_smem) + static_cast<uint32_t>(warp - 2) * 2u * EPI_TILE_BYTES;
+    const uint32_t st_mirror = st_direct + EPI_TILE_BYTES;
     int local = 0;
     const Epilogue& e = p.e;
-    const bool vec_d = ((e.ldd & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.D) & 15) == 0) &&
-                       ((e.strideD & 7) == 0);
     const bool vec_c = e.C && ((e.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.C) & 15) == 0) &&
                        ((e.strideC & 7) == 0);
+    const bool want_rsq = e.rowsq != nullptr;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++local) {
       int b, tm, tn;
       tile_coords(p, t, b, tm, tn);
@@ -344,64 +378,82 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag)) break;
       fence_after_sync();
-      const int row = tm * BM + quad * 32 + lane;
+      const int r0 = tm * BM + quad * 32;
+      const int row = r0 + lane;
       const float sc = e.scale ? e.alpha * e.scale[b] : e.alpha;
-      uint16_t* Db = e.D + static_cast<int64_t>(b) * e.strideD;
       const uint16_t* Cb = e.C ? e.C + static_cast<int64_t>(b) * e.strideC : nullptr;
       float rsq = 0.f;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
+        const int c0 = tn * BN + ch * 32;
+        // warp-uniform chunk classification
+        const bool outside = (c0 >= p.N) || (r0 >= p.M);
+        const bool below = p.sym && (c0 + 32 <= r0);
+        if (outside || below) continue;
+        const bool diag = p.sym && (c0 == r0);
         float v[32];
         __syncwarp();
         tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
-        const int col0 = tn * BN + ch * 32;
-        if (col0 < p.N && row < p.M) {
-          const bool full = col0 + 32 <= p.N;
-          float cv[32];
-          if (e.kind != 0) load_row32(Cb, e.ldc, row, col0, p.M, p.N, vec_c && full, e.d_half, cv);
-          uint16_t out[32];
+        float cv[32];
+        if (e.kind != 0) {
+          if (row < p.M) load_row32(Cb, e.ldc, row, c0, p.M, p.N, vec_c && (c0 + 32 <= p.N), e.d_half, cv);
+          else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = epi_value(p, e.kind, v[j], e.kind != 0 ? cv[j] : 0.f, sc, row, col0 + j);
-            out[j] = f32_to_h16(x, e.d_half);
-            const float xr = h16_to_f32(out[j], e.d_half);
-            if (col0 + j < p.N) rsq = fmaf(xr, xr, rsq);
+            for (int j = 0; j < 32; ++j) cv[j] = 0.f;
           }
-          if (!p.sym) {
-            if (full && vec_d) {
-              uint4* dst = reinterpret_cast<uint4*>(Db + static_cast<int64_t>(row) * e.ldd + col0);
+        }
+        uint32_t pk[16];
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 w;
-                w.x = out[q * 8 + 0] | (static_cast<uint32_t>(out[q * 8 + 1]) << 16);
-                w.y = out[q * 8 + 2] | (static_cast<uint32_t>(out[q * 8 + 3]) << 16);
-                w.z = out[q * 8 + 4] | (static_cast<uint32_t>(out[q * 8 + 5]) << 16);
-                w.w = out[q * 8 + 6] | (static_cast<uint32_t>(out[q * 8 + 7]) << 16);
-                dst[q] = w;
-              }
-            } else {
+        for (int j = 0; j < 32; j += 2) {
+          const float x0 = epi_value(p, e.kind, v[j], e.kind != 0 ? cv[j] : 0.f, sc, row, c0 + j);
+          const float x1 = epi_value(p, e.kind, v[j + 1], e.kind != 0 ? cv[j + 1] : 0.f, sc, row, c0 + j + 1);
+          const uint16_t h0 = f32_to_h16(x0, e.d_half), h1 = f32_to_h16(x1, e.d_half);
+          pk[j >> 1] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          if (want_rsq) {
+            const float y0 = h16_to_f32(h0, e.d_half), y1 = h16_to_f32(h1, e.d_half);
+            if (c0 + j < p.N) rsq = fmaf(y0, y0, rsq);
+            if (c0 + j + 1 < p.N) rsq = fmaf(y1, y1, rsq);
+          }
+        }
+        // the previous chunk's TMA stores must have read the staging tiles
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        if (!diag) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) Db[static_cast<int64_t>(row) * e.ldd + col0 + j] = out[j];
-            }
-          } else {
-            // symmetric: keep col >= row, write it and its mirror
+          for (int q = 0; q < 4; ++q)
+            st_shared_v4(st_direct + stage_off(lane, q * 8), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          if (p.sym) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const int col = col0 + j;
-              if (col < p.N && col >= row) {
-                Db[static_cast<int64_t>(row) * e.ldd + col] = out[j];
-                Db[static_cast<int64_t>(col) * e.ldd + row] = out[j];
-              }
+              const uint16_t h = static_cast<uint16_t>(j & 1 ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xFFFFu));
+              st_shared_u16(st_mirror + stage_off(j, lane), h);
             }
           }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j >= lane) {
+              const uint16_t h = static_cast<uint16_t>(j & 1 ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xFFFFu));
+              st_shared_u16(st_direct + stage_off(lane, j), h);
+              st_shared_u16(st_direct + stage_off(j, lane), h);
+            }
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmD, st_direct, c0, r0, b);
+          if (p.sym && !diag) tma_store_3d(&tmD, st_mirror, r0, c0, b);
+          bulk_commit();
         }
       }
       fence_before_sync();
       mbar_arrive(&tempty_bar[acc]);
-      if (e.rowsq && row < p.M)
+      if (want_rsq && row < p.M)
         e.rowsq[(static_cast<int64_t>(b) * p.tiles_n + tn) * p.M + row] = rsq;
     }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
   }
 
   fence_before_sync();
@@ -449,6 +501,25 @@ static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batc
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("gemm: cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
+    return -1;
+  }
+  return 0;
+}
+
+// Output map: rows of D (ldd apart) x columns, 32 x 32 boxes, 64-byte swizzle.
+static int make_store_map(CUtensorMap* map, const Epilogue& E, int M, int N, int batch) {
+  auto fn = encode_fn();
+  if (!fn) { set_error("gemm: cuTensorMapEncodeTiled unavailable"); return -1; }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(E.ldd) * 2, static_cast<cuuint64_t>(E.strideD) * 2};
+  if (batch == 1) strides[1] = strides[0] * dims[1];
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, E.d_half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, E.D, dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("gemm: output tensor map failed with code " + std::to_string(static_cast<int>(r)));
     return -1;
   }
   return 0;
@@ -513,10 +584,10 @@ int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K) {
-  (void)E;
   if (M < tc::BM || N < 128 || K < tc::BK) return false;
   if (!al16(A.ptr) || !al16(B.ptr)) return false;
   if ((A.ld & 7) || (B.ld & 7) || (A.stride & 7) || (B.stride & 7)) return false;
+  if (!al16(E.D) || (E.ldd & 7) || (E.strideD & 7)) return false;  // TMA store of the output
   return true;
 }
 
@@ -555,9 +626,10 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   p.err = device_error_word();
   if (!p.err) { set_error("gemm: no device error word"); return -1; }
 
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, md;
   if (tc::make_map(&ma, A, M, K, batch, tc::BM)) return -1;
   if (tc::make_map(&mb, B, N, K, batch, tc::BN)) return -1;
+  if (tc::make_store_map(&md, E, M, N, batch)) return -1;
 
   static int configured_dev = -1;
   int dev = 0;
@@ -569,7 +641,7 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
     configured_dev = dev;
   }
   const int grid = std::min(p.total_tiles, num_sms());
-  tc::gemm_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, p);
+  tc::gemm_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, md, p);
   count_launch();
   return check_launch("gemm_tc");
 }

@@ -32,31 +32,54 @@ static inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * 
 
 constexpr int kPool = 6;
 
+// Workspace of a multi-group call: six m x m buffers spanning every group's
+// matrices (so the m^3 products of all groups run as one batched GEMM), two
+// iterate buffers per group and the per-matrix scale factors.
 struct OrthoLayout {
-  int64_t pool_off, pool_stride, xa_off, xb_off, scal_off, total;
+  int m = 0, Stot = 0;
+  int64_t pool_stride = 0, scal_off = 0, total = 0;
+  std::vector<int64_t> xa_off, xb_off;
+  std::vector<int> s_off;
 };
 
-static OrthoLayout layout_for(int S, int r, int c) {
-  const int64_t m = std::min(r, c);
+static bool layout_multi(const OrthoGroup* g, int ng, OrthoLayout& L) {
+  if (ng <= 0) return false;
+  L.m = std::min(g[0].r, g[0].c);
+  L.Stot = 0;
+  for (int i = 0; i < ng; ++i) {
+    if (g[i].S <= 0 || g[i].r <= 0 || g[i].c <= 0 || std::min(g[i].r, g[i].c) != L.m) return false;
+    L.s_off.push_back(L.Stot);
+    L.Stot += g[i].S;
+  }
+  L.pool_stride = align_up(static_cast<int64_t>(L.Stot) * L.m * L.m * 2, 256);
+  int64_t off = kPool * L.pool_stride;
+  for (int i = 0; i < ng; ++i) {
+    const int64_t xbytes = align_up(static_cast<int64_t>(g[i].S) * g[i].r * g[i].c * 2, 256);
+    L.xa_off.push_back(off);
+    L.xb_off.push_back(off + xbytes);
+    off += 2 * xbytes;
+  }
+  L.scal_off = off;
+  L.total = off + align_up(static_cast<int64_t>(4) * L.Stot * 4, 256);
+  return true;
+}
+
+int64_t ortho_workspace_bytes_multi(const OrthoGroup* g, int ng) {
   OrthoLayout L;
-  L.pool_stride = align_up(static_cast<int64_t>(S) * m * m * 2, 256);
-  L.pool_off = 0;
-  const int64_t xbytes = align_up(static_cast<int64_t>(S) * r * c * 2, 256);
-  L.xa_off = L.pool_off + kPool * L.pool_stride;
-  L.xb_off = L.xa_off + xbytes;
-  L.scal_off = L.xb_off + xbytes;
-  L.total = L.scal_off + align_up(static_cast<int64_t>(4) * S * 4, 256);
-  return L;
+  if (!layout_multi(g, ng, L)) return -1;
+  return L.total;
 }
 
 int64_t ortho_workspace_bytes(int S, int r, int c) {
-  if (S <= 0 || r <= 0 || c <= 0) return -1;
-  return layout_for(S, r, c).total;
+  OrthoGroup g{nullptr, nullptr, nullptr, nullptr, S, r, c};
+  return ortho_workspace_bytes_multi(&g, 1);
 }
 
 // Per-matrix norm of the front's bf16 output, from its partial sums.
+// scal layout: [0, Stot) scale s, [Stot, 2 Stot) s^2, [2 Stot, 3 Stot) quintic divisor;
+// this group's matrices start at s_off.
 __global__ void norm_finalize_kernel(const float* __restrict__ partial, int nparts, int S, int mode, float eps,
-                                     float safety, float* __restrict__ scal) {
+                                     float safety, float* __restrict__ scal, int Stot, int s_off) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= S) return;
   float acc = 0.f;
@@ -65,11 +88,11 @@ __global__ void norm_finalize_kernel(const float* __restrict__ partial, int npar
   if (mode == 0) {
     // X.norm() of a bf16 tensor is returned in bf16; "+ eps" is again bf16 arithmetic
     const float nb = round_bf16(nrm);
-    scal[2 * S + s] = round_bf16(nb + eps);
+    scal[2 * Stot + s_off + s] = round_bf16(nb + eps);
   } else {
     const float sc = 1.0f / (nrm * safety + eps);
-    scal[s] = sc;
-    scal[S + s] = sc * sc;
+    scal[s_off + s] = sc;
+    scal[Stot + s_off + s] = sc * sc;
   }
 }
 
@@ -161,60 +184,81 @@ int prod(const Batch& b, const uint16_t* L, const uint16_t* Rs, Epilogue e, int 
 
 }  // namespace
 
-int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode, const float* coeffs,
-                  int T, const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
-                  int64_t ws_bytes, uint16_t* out, float* rowsq, cudaStream_t stream) {
-  if (S <= 0 || r <= 0 || c <= 0 || !U || !partial || !ws || !out || !rowsq || !coeffs) {
-    set_error("orthogonalize: bad arguments"); return -1;
+int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float* coeffs, int T, const int* resets,
+                        int nresets, float norm_eps, float norm_safety, void* ws, int64_t ws_bytes,
+                        cudaStream_t stream) {
+  if (ng <= 0 || !groups || !ws || !coeffs) { set_error("orthogonalize: bad arguments"); return -1; }
+  for (int i = 0; i < ng; ++i) {
+    const OrthoGroup& g = groups[i];
+    if (!g.U || !g.partial || !g.out || !g.rowsq || g.S <= 0 || g.r <= 0 || g.c <= 0) {
+      set_error("orthogonalize: bad arguments"); return -1;
+    }
   }
   if (mode != 0 && mode != 1) { set_error("orthogonalize: mode must be 0 or 1"); return -1; }
   if (T < 1 || T > 64) { set_error("orthogonalize: 1..64 steps"); return -1; }
   if (nresets < 0 || (nresets > 0 && !resets)) { set_error("orthogonalize: bad resets"); return -1; }
-  const OrthoLayout L = layout_for(S, r, c);
+  OrthoLayout L;
+  if (!layout_multi(groups, ng, L)) { set_error("orthogonalize: groups must share min(r, c)"); return -1; }
   if (ws_bytes < L.total) { set_error("orthogonalize: workspace too small"); return -1; }
   if (reinterpret_cast<uintptr_t>(ws) & 255) { set_error("orthogonalize: workspace must be 256-byte aligned"); return -1; }
 
-  Batch b;
-  b.S = S; b.r = r; b.c = c; b.m = std::min(r, c); b.n = std::max(r, c); b.tall = r > c;
-  b.half = mode == 1 ? 1 : 0;
-  b.rc = static_cast<int64_t>(r) * c; b.mm = static_cast<int64_t>(b.m) * b.m; b.st = stream;
+  const int half = mode == 1 ? 1 : 0;
+  std::vector<Batch> bg(ng);
+  for (int i = 0; i < ng; ++i) {
+    Batch& b = bg[i];
+    b.S = groups[i].S; b.r = groups[i].r; b.c = groups[i].c;
+    b.m = std::min(b.r, b.c); b.n = std::max(b.r, b.c); b.tall = b.r > b.c; b.half = half;
+    b.rc = static_cast<int64_t>(b.r) * b.c; b.mm = static_cast<int64_t>(b.m) * b.m; b.st = stream;
+  }
+  Batch ball = bg[0];  // all groups' m x m matrices as one batch
+  ball.S = L.Stot;
   uint8_t* base = static_cast<uint8_t*>(ws);
-  auto pool = [&](int i) { return reinterpret_cast<uint16_t*>(base + L.pool_off + i * L.pool_stride); };
-  uint16_t* Xa = reinterpret_cast<uint16_t*>(base + L.xa_off);
-  uint16_t* Xb = reinterpret_cast<uint16_t*>(base + L.xb_off);
+  const int64_t mm = ball.mm;
+  auto pool = [&](int i) { return reinterpret_cast<uint16_t*>(base + i * L.pool_stride); };
+  auto pool_g = [&](int i, int g) { return pool(i) + static_cast<int64_t>(L.s_off[g]) * mm; };
+  auto xa = [&](int g) { return reinterpret_cast<uint16_t*>(base + L.xa_off[g]); };
+  auto xb = [&](int g) { return reinterpret_cast<uint16_t*>(base + L.xb_off[g]); };
   float* scal = reinterpret_cast<float*>(base + L.scal_off);
 
-  const int64_t rc = b.rc;
-  const int nparts = normuon_front_parts(rc);
-  norm_finalize_kernel<<<(S + 127) / 128, 128, 0, stream>>>(partial, nparts, S, mode, norm_eps, norm_safety, scal);
-  count_launch();
-  if (int e = check_launch("norm_finalize")) return e;
+  for (int g = 0; g < ng; ++g) {
+    const int nparts = normuon_front_parts(bg[g].rc);
+    norm_finalize_kernel<<<(bg[g].S + 127) / 128, 128, 0, stream>>>(groups[g].partial, nparts, bg[g].S, mode,
+                                                                      norm_eps, norm_safety, scal, L.Stot, L.s_off[g]);
+    count_launch();
+    if (int e = check_launch("norm_finalize")) return e;
+  }
 
   int rc_ = 0;
   if (mode == 0) {
     const float a = coeffs[0], bb = coeffs[1], cc = coeffs[2];
-    const int gx = static_cast<int>(std::min<int64_t>((rc + 255) / 256, std::max(1, num_sms() * 8 / S)));
-    ns_normalize_kernel<<<dim3(gx, S), 256, 0, stream>>>(U, Xa, rc, scal + 2 * S);
-    count_launch();
-    if (int e = check_launch("ns_normalize")) return e;
-    uint16_t* X = Xa;
-    uint16_t* Y = Xb;
-    uint16_t* Am = pool(0);
-    uint16_t* Bm = pool(1);
+    std::vector<uint16_t*> X(ng), Y(ng);
+    for (int g = 0; g < ng; ++g) {
+      const int64_t rc = bg[g].rc;
+      const int S = bg[g].S;
+      const int gx = static_cast<int>(std::min<int64_t>((rc + 255) / 256, std::max(1, num_sms() * 8 / S)));
+      ns_normalize_kernel<<<dim3(gx, S), 256, 0, stream>>>(groups[g].U, xa(g), rc, scal + 2 * L.Stot + L.s_off[g]);
+      count_launch();
+      if (int e = check_launch("ns_normalize")) return e;
+      X[g] = xa(g);
+      Y[g] = xb(g);
+    }
     for (int t = 0; t < T; ++t) {
-      if ((rc_ = syrk(b, X, Am, nullptr))) return rc_;
+      for (int g = 0; g < ng; ++g)
+        if ((rc_ = syrk(bg[g], X[g], pool_g(0, g), nullptr))) return rc_;
       Epilogue eb;
       memset(&eb, 0, sizeof(eb));
-      eb.kind = 2; eb.beta = bb; eb.gamma = cc; eb.C = Am; eb.ldc = b.m; eb.strideC = b.mm; eb.D = Bm;
-      if ((rc_ = prod(b, Am, Am, eb, 1))) return rc_;
-      Epilogue ex;
-      memset(&ex, 0, sizeof(ex));
+      eb.kind = 2; eb.beta = bb; eb.gamma = cc; eb.C = pool(0); eb.ldc = ball.m; eb.strideC = mm; eb.D = pool(1);
+      if ((rc_ = prod(ball, pool(0), pool(0), eb, 1))) return rc_;
       const bool last = t == T - 1;
-      uint16_t* dst = last ? out : Y;
-      ex.kind = 3; ex.alpha = a; ex.C = X; ex.ldc = b.c; ex.strideC = rc; ex.D = dst;
-      ex.rowsq = last ? rowsq : nullptr;
-      if ((rc_ = apply_left(b, Bm, X, ex))) return rc_;
-      std::swap(X, Y);
+      for (int g = 0; g < ng; ++g) {
+        Epilogue ex;
+        memset(&ex, 0, sizeof(ex));
+        ex.kind = 3; ex.alpha = a; ex.C = X[g]; ex.ldc = bg[g].c; ex.strideC = bg[g].rc;
+        ex.D = last ? groups[g].out : Y[g];
+        ex.rowsq = last ? groups[g].rowsq : nullptr;
+        if ((rc_ = apply_left(bg[g], pool_g(1, g), X[g], ex))) return rc_;
+        std::swap(X[g], Y[g]);
+      }
     }
     return 0;
   }
@@ -231,57 +275,74 @@ int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, 
   };
   auto release = [&](int i) { if (i >= 0) used[i] = false; };
 
-  // normalised binary16 copy of the front output (the Gram iteration runs in
+  // normalised binary16 copy of each front output (the Gram iteration runs in
   // binary16: R, P and Q are bounded, and its 11-bit significand keeps the
   // Gram matrix far more accurate than bfloat16 at the same tensor-core rate)
-  {
+  std::vector<const uint16_t*> Xcur(ng);
+  for (int g = 0; g < ng; ++g) {
+    const int64_t rc = bg[g].rc;
+    const int S = bg[g].S;
     const int gx = static_cast<int>(std::min<int64_t>((rc / 8 + 255) / 256 + 1, std::max(1, num_sms() * 8 / S)));
-    to_half_scaled_kernel<<<dim3(gx, S), 256, 0, stream>>>(U, Xa, rc, scal);
+    to_half_scaled_kernel<<<dim3(gx, S), 256, 0, stream>>>(groups[g].U, xa(g), rc, scal + L.s_off[g]);
     count_launch();
     if (int e = check_launch("to_half_scaled")) return e;
+    Xcur[g] = xa(g);
   }
   int R = alloc();
-  if ((rc_ = syrk(b, Xa, pool(R), nullptr))) return rc_;
-  const uint16_t* Xcur = Xa;
+  for (int g = 0; g < ng; ++g)
+    if ((rc_ = syrk(bg[g], Xcur[g], pool_g(R, g), nullptr))) return rc_;
   int Q = -1;
   for (int t = 0; t < T; ++t) {
     const float a = coeffs[3 * t], bb = coeffs[3 * t + 1], cc = coeffs[3 * t + 2];
     if (is_reset(t)) {
-      uint16_t* Xn = (Xcur == Xa) ? Xb : Xa;
-      if ((rc_ = apply_left(b, pool(Q), Xcur, epi0(Xn, 0, 0, 1.0f, nullptr, 1)))) return rc_;
+      const int Rn = alloc();
+      for (int g = 0; g < ng; ++g) {
+        uint16_t* Xn = (Xcur[g] == xa(g)) ? xb(g) : xa(g);
+        if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], epi0(Xn, 0, 0, 1.0f, nullptr, 1)))) return rc_;
+        if ((rc_ = syrk(bg[g], Xn, pool_g(Rn, g), nullptr))) return rc_;
+        Xcur[g] = Xn;
+      }
       release(Q); Q = -1;
-      release(R); R = alloc();
-      if ((rc_ = syrk(b, Xn, pool(R), nullptr))) return rc_;
-      Xcur = Xn;
+      release(R); R = Rn;
     }
     const int P = alloc();
     Epilogue ep;
     memset(&ep, 0, sizeof(ep));
     ep.kind = 1; ep.alpha = a; ep.beta = bb; ep.gamma = cc; ep.d_half = 1;
-    ep.C = pool(R); ep.ldc = b.m; ep.strideC = b.mm; ep.D = pool(P);
-    if ((rc_ = prod(b, pool(R), pool(R), ep, 1))) return rc_;
+    ep.C = pool(R); ep.ldc = ball.m; ep.strideC = mm; ep.D = pool(P);
+    if ((rc_ = prod(ball, pool(R), pool(R), ep, 1))) return rc_;
     bool p_owned_by_q = false;
     if (Q < 0) {
       Q = P; p_owned_by_q = true;
     } else {
       const int Qn = alloc();
-      if ((rc_ = prod(b, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
+      if ((rc_ = prod(ball, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
       release(Q); Q = Qn;
     }
     const bool need_r = (t < T - 1) && !is_reset(t + 1);
     if (need_r) {
       const int T1 = alloc();
-      if ((rc_ = prod(b, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
+      if ((rc_ = prod(ball, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
       const int Rn = alloc();
-      if ((rc_ = prod(b, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
+      if ((rc_ = prod(ball, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
       release(T1); release(R); R = Rn;
     }
     if (!p_owned_by_q) release(P);
     if (R < 0 || Q < 0) { set_error("orthogonalize: workspace pool exhausted"); return -1; }
   }
-  Epilogue ef = epi0(out, 0, 0, 1.0f, nullptr, 0);  // o in bfloat16, as the reference returns it
-  ef.rowsq = rowsq;
-  return apply_left(b, pool(Q), Xcur, ef);
+  for (int g = 0; g < ng; ++g) {
+    Epilogue ef = epi0(groups[g].out, 0, 0, 1.0f, nullptr, 0);  // o in bfloat16, as the reference returns it
+    ef.rowsq = groups[g].rowsq;
+    if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], ef))) return rc_;
+  }
+  return 0;
+}
+
+int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode, const float* coeffs,
+                  int T, const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
+                  int64_t ws_bytes, uint16_t* out, float* rowsq, cudaStream_t stream) {
+  OrthoGroup g{U, partial, out, rowsq, S, r, c};
+  return orthogonalize_multi(&g, 1, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, ws, ws_bytes, stream);
 }
 
 }  // namespace b2o

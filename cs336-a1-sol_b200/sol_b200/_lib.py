@@ -51,6 +51,19 @@ class AdamwGroup(C.Structure):
     ]
 
 
+class OrthoGroup(C.Structure):
+    _fields_ = [
+        ("u", c_void_p),
+        ("partial", c_void_p),
+        ("out", c_void_p),
+        ("rowsq", c_void_p),
+        ("S", C.c_int32),
+        ("r", C.c_int32),
+        ("c", C.c_int32),
+        ("_pad", C.c_int32),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/b2o.h one to one
 SIGNATURES = {
     "b2o_version": (c_int, []),
@@ -71,6 +84,9 @@ SIGNATURES = {
     "b2o_orthogonalize": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, C.POINTER(c_float), c_int,
                                   C.POINTER(c_int), c_int, c_float, c_float, c_void_p, c_int64, c_void_p,
                                   c_void_p, c_void_p]),
+    "b2o_ortho_workspace_bytes_multi": (c_int64, [C.POINTER(OrthoGroup), c_int]),
+    "b2o_orthogonalize_multi": (c_int, [C.POINTER(OrthoGroup), c_int, c_int, C.POINTER(c_float), c_int,
+                                        C.POINTER(c_int), c_int, c_float, c_float, c_void_p, c_int64, c_void_p]),
     "b2o_normuon_apply_scratch_floats": (c_int64, [c_int, c_int]),
     "b2o_normuon_apply": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, C.POINTER(c_void_p),
                                   C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_void_p), c_int, c_float,

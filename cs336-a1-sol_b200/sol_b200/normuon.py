@@ -7,11 +7,13 @@ same constructor arguments, param-group keys, per-parameter state
 ``_orthogonalize_batch(U, ns_steps)`` hook (:366).
 
 Per exact-shape batch (the reference buckets by ``tuple(p.shape)``, :380-383)
-one step is four launches sequences of libb2o, with no stacking copies:
+one step is three library calls, with no stacking copies:
   front  (momentum lerp + Nesterov, :390-394)  -> u (S, r, c) bf16 + norm partials
   orthogonalise (:395; GEMMs on tcgen05)       -> o (S, r, c) bf16 + row sums of o^2
-  finish (v_row lerp + scale factors, :396-401) and
-  apply  (cautious WD, update, bf16 mantissa split, EMA; :402-424).
+  finish + apply (v_row lerp, scale factors, cautious WD, update, bf16
+         mantissa split, EMA; :396-424).
+The orthogonalisation of all batches that share m = min(r, c) is one call, so
+their m x m products run as single batched GEMMs.
 """
 from __future__ import annotations
 
@@ -54,6 +56,7 @@ class NorMuonGNS(torch.optim.Optimizer):
         self.norm_eps = float(norm_eps)
         self.norm_safety = float(norm_safety)
         self._ws = {}
+        self._ows = {}
         self._tables = {}
         self._owned = None         # set of id(param) this rank updates (sharded step), None = all
         self._ema = None           # EmaWeights folded into the apply pass (set when it arms)
@@ -102,28 +105,29 @@ class NorMuonGNS(torch.optim.Optimizer):
                 "rowsq": torch.zeros(S * ntn * r, dtype=torch.float32, device=device),
                 "scratch": torch.empty(lib.b2o_normuon_apply_scratch_floats(S, r), dtype=torch.float32,
                                        device=device),
-                "ortho": torch.empty(wbytes, dtype=torch.uint8, device=device),
+                "ortho_bytes": wbytes,
             }
             self._ws[key] = ws
         return ws
+
+    def _ortho_ws(self, device, key, nbytes):
+        """Orthogonaliser workspace shared by the batches of one m-class (uint8, 256-byte aligned)."""
+        buf = self._ows.get((device, key))
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            self._ows[(device, key)] = buf
+        return buf
 
     def _ortho(self, U, partial, S, r, c, ns_steps, out, ws):
         lib = _lib.load()
         coeffs, resets, nres = self._table(ns_steps)
         mode = 0 if self.orthogonalizer == "quintic" else 1
-        ev = self._timing_events
-        if ev is not None:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record()
+        ortho = self._ortho_ws(U.device, ("single", S, r, c), ws["ortho_bytes"])
         rc = lib.b2o_orthogonalize(U.data_ptr(), partial.data_ptr(), S, r, c, mode, coeffs, ns_steps, resets,
-                                   nres, self.norm_eps, self.norm_safety, ws["ortho"].data_ptr(),
-                                   ws["ortho"].numel(), out.data_ptr(), ws["rowsq"].data_ptr(),
+                                   nres, self.norm_eps, self.norm_safety, ortho.data_ptr(),
+                                   ortho.numel(), out.data_ptr(), ws["rowsq"].data_ptr(),
                                    _lib.stream_ptr(U.device))
         _lib.check(rc, "orthogonalize")
-        if ev is not None:
-            e1 = torch.cuda.Event(enable_timing=True)
-            e1.record()
-            ev.append((e0, e1))
 
     def _hook_overridden(self):
         return ("_orthogonalize_batch" in self.__dict__ or
@@ -138,7 +142,8 @@ class NorMuonGNS(torch.optim.Optimizer):
             st["mant_rem"] = torch.zeros_like(p)
         return st
 
-    def _step_batch(self, params, shape, group):
+    def _front(self, params, shape, group):
+        """Momentum + Nesterov for one exact-shape batch; returns the batch record."""
         lib = _lib.load()
         p0 = params[0]
         _lib.require_cuda(p0, "NorMuonGNS.step")
@@ -151,30 +156,49 @@ class NorMuonGNS(torch.optim.Optimizer):
             if p.grad.dtype != p.dtype or not p.is_contiguous() or not p.grad.is_contiguous():
                 raise ValueError("NorMuonGNS needs contiguous params and grads of the param dtype")
         states = [self._init_state(p) for p in params]
-        dt = _lib.dtype_code(p0.dtype)
         ws = self._workspace(dev, S, r, c)
-        stream = _lib.stream_ptr(dev)
-        beta, beta2 = float(group["momentum"]), float(group["beta2"])
-        lr, wd = float(group["lr"]), float(group["weight_decay"])
-        ns_steps, nesterov = int(group["ns_steps"]), bool(group["nesterov"])
-
+        beta = float(group["momentum"])
         grads = _lib.ptr_array([p.grad.data_ptr() for p in params])
         bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in states])
-        rc = lib.b2o_normuon_front(grads, bufs, S, r, c, dt, 1.0 - beta, beta, int(nesterov),
-                                   ws["u"].data_ptr(), ws["partial"].data_ptr(), stream)
+        rc = lib.b2o_normuon_front(grads, bufs, S, r, c, _lib.dtype_code(p0.dtype), 1.0 - beta, beta,
+                                   int(bool(group["nesterov"])), ws["u"].data_ptr(), ws["partial"].data_ptr(),
+                                   _lib.stream_ptr(dev))
         _lib.check(rc, "normuon_front")
+        return dict(params=params, states=states, ws=ws, S=S, r=r, c=c, dev=dev, o=ws["o"])
 
-        if self._hook_overridden():
-            o = self._orthogonalize_batch(ws["u"], ns_steps)
-            o = o.to(torch.bfloat16).contiguous()
-            ntn = (c + 255) // 256
-            rs = ws["rowsq"].view(S, ntn, r)
-            rs.zero_()
-            rs[:, 0, :] = o.float().pow(2).sum(dim=-1)
-        else:
-            o = ws["o"]
-            self._ortho(ws["u"], ws["partial"], S, r, c, ns_steps, o, ws)
+    def _ortho_class(self, batches, ns_steps):
+        """Orthogonalises every batch of one m = min(r, c) class with one library call."""
+        lib = _lib.load()
+        dev = batches[0]["dev"]
+        coeffs, resets, nres = self._table(ns_steps)
+        mode = 0 if self.orthogonalizer == "quintic" else 1
+        groups = (_lib.OrthoGroup * len(batches))()
+        for i, b in enumerate(batches):
+            ws = b["ws"]
+            groups[i] = _lib.OrthoGroup(ws["u"].data_ptr(), ws["partial"].data_ptr(), ws["o"].data_ptr(),
+                                        ws["rowsq"].data_ptr(), b["S"], b["r"], b["c"], 0)
+        key = ("multi",) + tuple((b["S"], b["r"], b["c"]) for b in batches)
+        nbytes = lib.b2o_ortho_workspace_bytes_multi(groups, len(batches))
+        ortho = self._ortho_ws(dev, key, nbytes)
+        ev = self._timing_events
+        if ev is not None:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        rc = lib.b2o_orthogonalize_multi(groups, len(batches), mode, coeffs, ns_steps, resets, nres, self.norm_eps,
+                                         self.norm_safety, ortho.data_ptr(), ortho.numel(), _lib.stream_ptr(dev))
+        _lib.check(rc, "orthogonalize_multi")
+        if ev is not None:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            ev.append((e0, e1))
 
+    def _apply(self, b, group):
+        lib = _lib.load()
+        params, states, ws = b["params"], b["states"], b["ws"]
+        S, r, c, dev = b["S"], b["r"], b["c"], b["dev"]
+        p0 = params[0]
+        beta2 = float(group["beta2"])
+        lr, wd = float(group["lr"]), float(group["weight_decay"])
         mt = self.bf16_master and p0.dtype == torch.bfloat16
         pptr = _lib.ptr_array([p.data_ptr() for p in params])
         rems = _lib.ptr_array([st["mant_rem"].data_ptr() for st in states]) if mt else None
@@ -188,10 +212,32 @@ class NorMuonGNS(torch.optim.Optimizer):
                     self._ema._mark(p)
         wd_on = 1 if wd else 0
         shape_scale = math.sqrt(max(1.0, r / c))
-        rc = lib.b2o_normuon_apply(o.data_ptr(), ws["rowsq"].data_ptr(), S, r, c, pptr, rems, emas, vrows, dt,
-                                   -lr, lr * wd, 1.0 - lr * wd, wd_on, int(bool(self.cautious_wd and wd)),
-                                   shape_scale, 1.0 - beta2, self._ema_weight, ws["scratch"].data_ptr(), stream)
+        rc = lib.b2o_normuon_apply(b["o"].data_ptr(), ws["rowsq"].data_ptr(), S, r, c, pptr, rems, emas, vrows,
+                                   _lib.dtype_code(p0.dtype), -lr, lr * wd, 1.0 - lr * wd, wd_on,
+                                   int(bool(self.cautious_wd and wd)), shape_scale, 1.0 - beta2, self._ema_weight,
+                                   ws["scratch"].data_ptr(), _lib.stream_ptr(dev))
         _lib.check(rc, "normuon_apply")
+
+    def _step_group(self, batches, group):
+        ns_steps = int(group["ns_steps"])
+        recs = [self._front(params, shape, group) for shape, params in batches]
+        if self._hook_overridden():
+            for b in recs:
+                S, r, c = b["S"], b["r"], b["c"]
+                o = self._orthogonalize_batch(b["ws"]["u"], ns_steps).to(torch.bfloat16).contiguous()
+                ntn = (c + 255) // 256
+                rs = b["ws"]["rowsq"].view(S, ntn, r)
+                rs.zero_()
+                rs[:, 0, :] = o.float().pow(2).sum(dim=-1)
+                b["o"] = o
+        else:
+            classes = OrderedDict()
+            for b in recs:
+                classes.setdefault((b["dev"], min(b["r"], b["c"])), []).append(b)
+            for members in classes.values():
+                self._ortho_class(members, ns_steps)
+        for b in recs:
+            self._apply(b, group)
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -207,7 +253,8 @@ class NorMuonGNS(torch.optim.Optimizer):
                 if self._owned is not None and id(p) not in self._owned:
                     continue
                 by_shape.setdefault(tuple(p.shape), []).append(p)
-            for shape, params in by_shape.items():
-                for i in range(0, len(params), MAX_BATCH):
-                    self._step_batch(params[i:i + MAX_BATCH], shape, group)
+            batches = [(shape, params[i:i + MAX_BATCH]) for shape, params in by_shape.items()
+                       for i in range(0, len(params), MAX_BATCH)]
+            if batches:
+                self._step_group(batches, group)
         return loss

@@ -128,6 +128,23 @@ int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r,
                       void* d_ws, int64_t ws_bytes, uint16_t* d_out, float* d_rowsq,
                       void* stream);
 
+/* Several shape-batches that share m = min(r, c) in one call: the m x m
+ * products of every group run as single batched GEMMs (the reference calls
+ * its orthogonaliser once per exact shape, sol_modules.py:380-395; grouping by
+ * m only changes launch granularity, not any matrix's arithmetic). */
+typedef struct {
+  const uint16_t* u;      /* front output (S, r, c) bf16            */
+  const float* partial;   /* front sum-of-squares partials          */
+  uint16_t* out;          /* o (S, r, c) bf16                        */
+  float* rowsq;           /* S * r * ceil(c/256) floats              */
+  int32_t S, r, c, _pad;
+} b2o_ortho_group;
+int64_t b2o_ortho_workspace_bytes_multi(const b2o_ortho_group* groups, int ngroups);
+int b2o_orthogonalize_multi(const b2o_ortho_group* groups, int ngroups, int mode,
+                            const float* coeffs, int T, const int* resets, int nresets,
+                            float norm_eps, float norm_safety, void* d_ws, int64_t ws_bytes,
+                            void* stream);
+
 /* Finish + apply (sol_modules.py:396-424): v_row lerp, row/matrix scaling,
  * shape scale, cautious weight decay, update, bf16 mantissa split, EMA.
  *   params/rems/emas/vrows: S pointers each (rems/emas may be NULL arrays)

@@ -84,7 +84,9 @@ def test_adamw_matches_torch_fused_cuda(cuda, dtype):
 
 
 def test_adamw_master_mode_vs_oracle(cuda):
-    """bf16 params + bf16 remainder + fp32 moments + cautious decay vs the CPU restatement."""
+    """bf16 params + bf16 remainder + fp32 moments + cautious decay vs the CPU
+    restatement, one step at a time from identical state (6 steps: the oracle's
+    state is copied into the engine before each step)."""
     g = torch.Generator().manual_seed(1)
     shapes = [(512, 96), (1000,), (3, 40, 24)]
     init = [torch.randn(s, generator=g) * 0.02 for s in shapes]
@@ -99,23 +101,30 @@ def test_adamw_master_mode_vs_oracle(cuda):
             gr[..., :3] *= 10
             gr = gr.to(torch.bfloat16)
             a.grad, b.grad = gr.cuda(), gr.clone()
+        if step > 0:  # identical starting state
+            for a, b, st in zip(pg, pc, orc.state):
+                so = ours.state[a]
+                a.data.copy_(b.data)
+                so["mant_rem"].copy_(st["rem"])
+                so["exp_avg"].copy_(st["m"])
+                so["exp_avg_sq"].copy_(st["v"])
+        w_before = [b.data.float() + (st["rem"].float() if st["rem"] is not None else 0) for b, st in zip(pc, orc.state)]
         ours.step()
         orc.step()
-    torch.cuda.synchronize()
-    for a, b, st in zip(pg, pc, orc.state):
-        so = ours.state[a]
-        assert_f32_ulps(so["exp_avg"], st["m"], what="exp_avg")
-        assert_f32_ulps(so["exp_avg_sq"], st["v"], what="exp_avg_sq")
-        w_ours = a.data.float().cpu() + so["mant_rem"].float().cpu()
-        w_orc = b.data.float() + st["rem"].float()
-        # bf16 parameter + bf16 remainder resolves |w| to about 2^-16 |w| (16
-        # significant bits). The bias corrections use powf on the GPU and
-        # torch.pow on the CPU (an ulp apart at most); such one-ulp differences
-        # of the fp32 weight can move the remainder's own bf16 rounding by one
-        # step, so the pair agrees to two remainder steps.
-        tol = 2.0 ** -15 * w_orc.abs() + 4 * _ulp_f32(w_orc)
-        assert ((w_ours - w_orc).abs() <= tol).all(), "reconstructed weight"
-        assert_bf16_close(a.data, b.data, "bf16 parameter", min_exact=0.999)
+        torch.cuda.synchronize()
+        for a, b, st, wb in zip(pg, pc, orc.state, w_before):
+            so = ours.state[a]
+            assert_f32_ulps(so["exp_avg"], st["m"], what="exp_avg")
+            assert_f32_ulps(so["exp_avg_sq"], st["v"], what="exp_avg_sq")
+            w_ours = a.data.float().cpu() + so["mant_rem"].float().cpu()
+            w_orc = b.data.float() + st["rem"].float()
+            # bf16 parameter + bf16 remainder resolves w to about 2^-16 |w|; the
+            # bias corrections use powf on the GPU and torch.pow on the CPU (an ulp
+            # apart at most), which moves the update by a few 1e-7 of itself, and
+            # such a difference can move the remainder's bf16 rounding by one step.
+            tol = 2.0 ** -15 * w_orc.abs() + 5e-7 * (w_orc - wb).abs() + 4 * _ulp_f32(w_orc)
+            assert ((w_ours - w_orc).abs() <= tol).all(), f"reconstructed weight, step {step}"
+            assert_bf16_close(a.data, b.data, "bf16 parameter", min_exact=0.999)
 
 
 def test_mantissa_split_is_bit_exact(cuda):
