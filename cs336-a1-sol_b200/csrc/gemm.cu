@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 namespace b2o {
 
@@ -34,10 +35,12 @@ constexpr int B_BYTES = BN * BK * 2;            // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 columns
-// Epilogue staging: per epilogue warp two 32x32 16-bit tiles (direct and
-// mirrored), 64-byte rows in the TMA 64-byte swizzle, written by TMA stores.
+// Epilogue staging: per epilogue warp two slots of two 32x32 16-bit tiles
+// (direct and mirrored), 64-byte rows in the TMA 64-byte swizzle, written by
+// TMA stores; while one slot's stores drain the next chunk fills the other.
 constexpr int EPI_TILE_BYTES = 32 * 32 * 2;
-constexpr int EPI_BYTES = 4 * 2 * EPI_TILE_BYTES;  // 16 KB
+constexpr int EPI_WARP_BYTES = 2 * 2 * EPI_TILE_BYTES;  // 8 KB
+constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;           // 32 KB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
@@ -109,6 +112,7 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Byte offset of 16-bit element (row, col) in a 32x32 staging tile stored with
@@ -154,6 +158,20 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                    smem_u32(bar))
                : "memory");
 }
+// Issues a 32-column TMEM load into r (completes at tmem_ld_wait()).
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* out) {
   uint32_t r[32];
   asm volatile(
@@ -214,20 +232,33 @@ __device__ __forceinline__ void load_row32(const uint16_t* base, int64_t ld, int
   }
 }
 
-__device__ __forceinline__ float epi_value(const Params& p, int kind, float acc, float c, float sc, int row,
-                                           int col) {
-  switch (kind) {
-    case 0:
-      return acc * sc;
-    case 1:
-      return fmaf(p.e.gamma, acc, fmaf(p.e.beta, c, row == col ? p.e.alpha : 0.f));
-    case 2:
-      return round_bf16(round_bf16(p.e.beta * c) + round_bf16(p.e.gamma * round_bf16(acc)));
-    default:
-      return round_bf16(round_bf16(p.e.alpha * c) + round_bf16(acc));
+template <int KIND>
+__device__ __forceinline__ float epi_value(const Params& p, float acc, float c, float sc, int row, int col) {
+  if (KIND == 0) return acc * sc;
+  if (KIND == 1) return fmaf(p.e.gamma, acc, fmaf(p.e.beta, c, row == col ? p.e.alpha : 0.f));
+  if (KIND == 2) return round_bf16(round_bf16(p.e.beta * c) + round_bf16(p.e.gamma * round_bf16(acc)));
+  return round_bf16(round_bf16(p.e.alpha * c) + round_bf16(acc));
+}
+// Two values rounded to the 16-bit output type, packed low/high.
+template <int DHALF>
+__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
+  if (DHALF) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    return *reinterpret_cast<const uint32_t*>(&h);
   }
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <int DHALF>
+__device__ __forceinline__ float unpack_lo(uint32_t w) {
+  return DHALF ? f16_to_f32(static_cast<uint16_t>(w & 0xFFFFu)) : bf16_to_f32(static_cast<uint16_t>(w & 0xFFFFu));
+}
+template <int DHALF>
+__device__ __forceinline__ float unpack_hi(uint32_t w) {
+  return DHALF ? f16_to_f32(static_cast<uint16_t>(w >> 16)) : bf16_to_f32(static_cast<uint16_t>(w >> 16));
 }
 
+template <int KIND, int DHALF, int SYM, int RSQ>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ Params p) {
@@ -364,13 +395,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     // below the diagonal, store chunks above it twice (direct and mirrored)
     // and symmetrise the diagonal chunk in shared memory before one store.
     const int quad = warp & 3;
-    const uint32_t st_direct = smem_u32(epi_smem) + static_cast<uint32_t>(warp - 2) * 2u * EPI_TILE_BYTES;
-    const uint32_t st_mirror = st_direct + EPI_TILE_BYTES;
+    const uint32_t st_base = smem_u32(epi_smem) + static_cast<uint32_t>(warp - 2) * EPI_WARP_BYTES;
     int local = 0;
     const Epilogue& e = p.e;
     const bool vec_c = e.C && ((e.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.C) & 15) == 0) &&
                        ((e.strideC & 7) == 0);
-    const bool want_rsq = e.rowsq != nullptr;
+    constexpr bool want_rsq = RSQ != 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++local) {
       int b, tm, tn;
       tile_coords(p, t, b, tm, tn);
@@ -383,20 +413,34 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float sc = e.scale ? e.alpha * e.scale[b] : e.alpha;
       const uint16_t* Cb = e.C ? e.C + static_cast<int64_t>(b) * e.strideC : nullptr;
       float rsq = 0.f;
-#pragma unroll 1
+      // chunks this warp moves out (warp-uniform): inside the matrix and, for
+      // symmetric outputs, on or above the diagonal
+      uint32_t todo = 0;
+#pragma unroll
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int c0 = tn * BN + ch * 32;
-        // warp-uniform chunk classification
-        const bool outside = (c0 >= p.N) || (r0 >= p.M);
-        const bool below = p.sym && (c0 + 32 <= r0);
-        if (outside || below) continue;
-        const bool diag = p.sym && (c0 == r0);
-        float v[32];
+        const bool skip = (c0 >= p.N) || (r0 >= p.M) || (SYM && (c0 + 32 <= r0));
+        if (!skip) todo |= 1u << ch;
+      }
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
+      uint32_t cur[32], nxt[32];
+      int ch = todo ? __ffs(todo) - 1 : -1;
+      if (ch >= 0) {
         __syncwarp();
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + ch * 32, v);
+        tmem_ld32_issue(tbase + ch * 32, cur);
+        tmem_ld_wait();
+      }
+      int slot = 0;
+#pragma unroll 1
+      while (ch >= 0) {
+        const uint32_t rest = todo & ~((2u << ch) - 1u);
+        const int nch = rest ? __ffs(rest) - 1 : -1;
+        if (nch >= 0) tmem_ld32_issue(tbase + nch * 32, nxt);  // overlaps this chunk's work
+        const int c0 = tn * BN + ch * 32;
+        const bool diag = SYM && (c0 == r0);
         float cv[32];
-        if (e.kind != 0) {
-          if (row < p.M) load_row32(Cb, e.ldc, row, c0, p.M, p.N, vec_c && (c0 + 32 <= p.N), e.d_half, cv);
+        if (KIND != 0) {
+          if (row < p.M) load_row32(Cb, e.ldc, row, c0, p.M, p.N, vec_c && (c0 + 32 <= p.N), DHALF, cv);
           else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) cv[j] = 0.f;
@@ -405,24 +449,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float x0 = epi_value(p, e.kind, v[j], e.kind != 0 ? cv[j] : 0.f, sc, row, c0 + j);
-          const float x1 = epi_value(p, e.kind, v[j + 1], e.kind != 0 ? cv[j + 1] : 0.f, sc, row, c0 + j + 1);
-          const uint16_t h0 = f32_to_h16(x0, e.d_half), h1 = f32_to_h16(x1, e.d_half);
-          pk[j >> 1] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+          const float x0 = epi_value<KIND>(p, __uint_as_float(cur[j]), KIND != 0 ? cv[j] : 0.f, sc, row, c0 + j);
+          const float x1 =
+              epi_value<KIND>(p, __uint_as_float(cur[j + 1]), KIND != 0 ? cv[j + 1] : 0.f, sc, row, c0 + j + 1);
+          pk[j >> 1] = pack2<DHALF>(x0, x1);
           if (want_rsq) {
-            const float y0 = h16_to_f32(h0, e.d_half), y1 = h16_to_f32(h1, e.d_half);
+            const float y0 = unpack_lo<DHALF>(pk[j >> 1]), y1 = unpack_hi<DHALF>(pk[j >> 1]);
             if (c0 + j < p.N) rsq = fmaf(y0, y0, rsq);
             if (c0 + j + 1 < p.N) rsq = fmaf(y1, y1, rsq);
           }
         }
-        // the previous chunk's TMA stores must have read the staging tiles
-        if (lane == 0) bulk_wait_read0();
+        const uint32_t st_direct = st_base + static_cast<uint32_t>(slot) * 2u * EPI_TILE_BYTES;
+        const uint32_t st_mirror = st_direct + EPI_TILE_BYTES;
+        // the stores issued from this slot two chunks ago must have read it
+        if (lane == 0) bulk_wait_read1();
         __syncwarp();
         if (!diag) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             st_shared_v4(st_direct + stage_off(lane, q * 8), pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          if (p.sym) {
+          if (SYM) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const uint16_t h = static_cast<uint16_t>(j & 1 ? (pk[j >> 1] >> 16) : (pk[j >> 1] & 0xFFFFu));
@@ -443,9 +489,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           tma_store_3d(&tmD, st_direct, c0, r0, b);
-          if (p.sym && !diag) tma_store_3d(&tmD, st_mirror, r0, c0, b);
+          if (SYM && !diag) tma_store_3d(&tmD, st_mirror, r0, c0, b);
           bulk_commit();
         }
+        slot ^= 1;
+        if (nch >= 0) {
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+        }
+        ch = nch;
       }
       fence_before_sync();
       mbar_arrive(&tempty_bar[acc]);
@@ -459,6 +512,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_before_sync();
   __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicOr(p.err, kErrWaitTimeout);
+  (void)DHALF;
   if (warp == 1) {
     __syncwarp();
     fence_after_sync();
@@ -631,17 +685,36 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   if (tc::make_map(&mb, B, N, K, batch, tc::BN)) return -1;
   if (tc::make_store_map(&md, E, M, N, batch)) return -1;
 
-  static int configured_dev = -1;
+  using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const tc::Params);
+  // [kind][d_half][sym][rowsq]; invalid combinations are rejected above
+  static const KernelFn table[4][2][2][2] = {
+      {{{tc::gemm_tc_kernel<0, 0, 0, 0>, tc::gemm_tc_kernel<0, 0, 0, 1>}, {tc::gemm_tc_kernel<0, 0, 1, 0>, nullptr}},
+       {{tc::gemm_tc_kernel<0, 1, 0, 0>, tc::gemm_tc_kernel<0, 1, 0, 1>}, {tc::gemm_tc_kernel<0, 1, 1, 0>, nullptr}}},
+      {{{tc::gemm_tc_kernel<1, 0, 0, 0>, tc::gemm_tc_kernel<1, 0, 0, 1>}, {tc::gemm_tc_kernel<1, 0, 1, 0>, nullptr}},
+       {{tc::gemm_tc_kernel<1, 1, 0, 0>, tc::gemm_tc_kernel<1, 1, 0, 1>}, {tc::gemm_tc_kernel<1, 1, 1, 0>, nullptr}}},
+      {{{tc::gemm_tc_kernel<2, 0, 0, 0>, tc::gemm_tc_kernel<2, 0, 0, 1>}, {tc::gemm_tc_kernel<2, 0, 1, 0>, nullptr}},
+       {{nullptr, nullptr}, {nullptr, nullptr}}},
+      {{{tc::gemm_tc_kernel<3, 0, 0, 0>, tc::gemm_tc_kernel<3, 0, 0, 1>}, {tc::gemm_tc_kernel<3, 0, 1, 0>, nullptr}},
+       {{nullptr, nullptr}, {nullptr, nullptr}}},
+  };
+  const KernelFn fn = table[E.kind][E.d_half ? 1 : 0][sym ? 1 : 0][E.rowsq ? 1 : 0];
+  if (!fn) { set_error("gemm: unsupported epilogue combination"); return -1; }
+  static std::mutex attr_mu;
+  static std::vector<std::pair<int, const void*>> configured;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_dev != dev) {
-    cudaError_t ce = cudaFuncSetAttribute(tc::gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          tc::SMEM_BYTES);
-    if (ce != cudaSuccess) { set_error(std::string("gemm: smem attribute: ") + cudaGetErrorString(ce)); return ce; }
-    configured_dev = dev;
+  {
+    std::lock_guard<std::mutex> lk(attr_mu);
+    const std::pair<int, const void*> key{dev, reinterpret_cast<const void*>(fn)};
+    if (std::find(configured.begin(), configured.end(), key) == configured.end()) {
+      cudaError_t ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+      if (ce != cudaSuccess) { set_error(std::string("gemm: smem attribute: ") + cudaGetErrorString(ce)); return ce; }
+      configured.push_back(key);
+    }
   }
   const int grid = std::min(p.total_tiles, num_sms());
-  tc::gemm_tc_kernel<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, md, p);
+  fn<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, md, p);
   count_launch();
   return check_launch("gemm_tc");
 }
