@@ -28,11 +28,22 @@ namespace b2o {
 
 namespace tc {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;     // BM: rows of one CTA's accumulator
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
-constexpr int B_BYTES = BN * BK * 2;            // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+// PAIR = 1: one CTA computes a 128 x 256 tile (4 stages of 16 + 32 KB).
+// PAIR = 2: a CTA pair (cluster of 2, tcgen05 cta_group::2) computes a
+// 256 x 256 tile; each CTA stages its 128 rows of A and its 128 columns of B
+// (6 stages of 16 + 16 KB), halving the operand bytes each SM pulls per MMA.
+template <int PAIR> struct Geo {
+  static constexpr int B_ROWS = BN / PAIR;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
+  static constexpr int TILE_M = BM * PAIR;
+};
+constexpr int STAGE_AREA = 4 * (A_BYTES + BN * BK * 2);  // 192 KB for either geometry
+static_assert(Geo<1>::STAGES * Geo<1>::STAGE_BYTES == STAGE_AREA, "stage area");
+static_assert(Geo<2>::STAGES * Geo<2>::STAGE_BYTES == STAGE_AREA, "stage area");
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 columns
 // Epilogue staging: per epilogue warp two slots of two 32x32 16-bit tiles
@@ -41,11 +52,12 @@ constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 col
 constexpr int EPI_TILE_BYTES = 32 * 32 * 2;
 constexpr int EPI_WARP_BYTES = 2 * 2 * EPI_TILE_BYTES;  // 8 KB
 constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;           // 32 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_BYTES = STAGE_AREA + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct Params {
   int M, N, K, batch;
+  int tile_m;  // rows per output tile: 128 (one CTA) or 256 (CTA pair)
   int a_kmajor, b_kmajor, sym, in_half;
   int tiles_m, tiles_n, tiles_per_batch, total_tiles, nk;
   Epilogue e;
@@ -127,6 +139,57 @@ __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t caddr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr), "r"(bytes) : "memory");
+}
+// TMA load whose completion is signalled on an mbarrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                                 uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(mbar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on the mbarrier at this offset in both CTAs of the pair once all
+// prior cta_group::2 MMAs of this thread have completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 __device__ __forceinline__ void fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -201,7 +264,7 @@ __device__ __forceinline__ void tile_coords(const Params& p, int t, int& b, int&
   }
   tn = 0;
   while (true) {
-    const int cnt = min(p.tiles_m, (tn * BN + BN - 1) / BM + 1);
+    const int cnt = min(p.tiles_m, (tn * BN + BN - 1) / p.tile_m + 1);
     if (local < cnt) { tm = local; return; }
     local -= cnt;
     ++tn;
@@ -258,13 +321,16 @@ __device__ __forceinline__ float unpack_hi(uint32_t w) {
   return DHALF ? f16_to_f32(static_cast<uint16_t>(w >> 16)) : bf16_to_f32(static_cast<uint16_t>(w >> 16));
 }
 
-template <int KIND, int DHALF, int SYM, int RSQ>
+template <int KIND, int DHALF, int SYM, int RSQ, int PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ Params p) {
+  using G = Geo<PAIR>;
+  constexpr int STAGES = G::STAGES;
+  constexpr int STAGE_BYTES = G::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
+  uint8_t* epi_smem = smem + STAGE_AREA;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
@@ -275,23 +341,36 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR == 2 ? cluster_rank() : 0u;  // 0 = the CTA that issues the MMAs
+  const int unit = blockIdx.x / PAIR;                       // tile-schedule slot (CTA or CTA pair)
+  const int nunits = gridDim.x / PAIR;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 128); }
+    // full: one expect-tx arrival per CTA of the pair (counted on the MMA CTA);
+    // tempty: every epilogue thread of the pair releases the accumulator
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], PAIR); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 128 * PAIR); }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (PAIR == 2) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(TMEM_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   fence_before_sync();
   __syncthreads();
+  if (PAIR == 2) cluster_sync();  // the peer's barriers exist before any remote arrival
   fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -304,34 +383,55 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int s = 0; s < STAGES; ++s) last_phase[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int t = unit; t < p.total_tiles && ok; t += nunits) {
         int b, tm, tn;
         tile_coords(p, t, b, tm, tn);
+        const int arow = tm * G::TILE_M + static_cast<int>(rank) * BM;    // this CTA's rows of A
+        const int bcol = tn * BN + static_cast<int>(rank) * G::B_ROWS;     // this CTA's columns of B
         for (int kb = 0; kb < p.nk; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t a_dst = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t b_dst = a_dst + A_BYTES;
-          mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
-          if (p.a_kmajor) {
-            tma_load_3d(a_dst, &tmA, kb * BK, tm * BM, b, &full_bar[stage]);
-          } else {
-            tma_load_3d(a_dst, &tmA, tm * BM, kb * BK, b, &full_bar[stage]);
-            tma_load_3d(a_dst + 8192, &tmA, tm * BM + 64, kb * BK, b, &full_bar[stage]);
-          }
-          if (p.b_kmajor) {
-            tma_load_3d(b_dst, &tmB, kb * BK, tn * BN, b, &full_bar[stage]);
-          } else {
+          if (PAIR == 1) {
+            mbar_expect_tx(&full_bar[stage], STAGE_BYTES);
+            if (p.a_kmajor) {
+              tma_load_3d(a_dst, &tmA, kb * BK, arow, b, &full_bar[stage]);
+            } else {
+              tma_load_3d(a_dst, &tmA, arow, kb * BK, b, &full_bar[stage]);
+              tma_load_3d(a_dst + 8192, &tmA, arow + 64, kb * BK, b, &full_bar[stage]);
+            }
+            if (p.b_kmajor) {
+              tma_load_3d(b_dst, &tmB, kb * BK, bcol, b, &full_bar[stage]);
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              tma_load_3d(b_dst + q * 8192, &tmB, tn * BN + q * 64, kb * BK, b, &full_bar[stage]);
+              for (int q = 0; q < G::B_ROWS / 64; ++q)
+                tma_load_3d(b_dst + q * 8192, &tmB, bcol + q * 64, kb * BK, b, &full_bar[stage]);
+            }
+          } else {
+            const uint32_t fb = map_to_rank(smem_u32(&full_bar[stage]), 0);
+            mbar_expect_tx_cluster(fb, STAGE_BYTES);
+            if (p.a_kmajor) {
+              tma_load_3d_pair(a_dst, &tmA, kb * BK, arow, b, fb);
+            } else {
+              tma_load_3d_pair(a_dst, &tmA, arow, kb * BK, b, fb);
+              tma_load_3d_pair(a_dst + 8192, &tmA, arow + 64, kb * BK, b, fb);
+            }
+            if (p.b_kmajor) {
+              tma_load_3d_pair(b_dst, &tmB, kb * BK, bcol, b, fb);
+            } else {
+#pragma unroll
+              for (int q = 0; q < G::B_ROWS / 64; ++q)
+                tma_load_3d_pair(b_dst + q * 8192, &tmB, bcol + q * 64, kb * BK, b, fb);
+            }
           }
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      if (!ok || *abort_flag) {
-        // Drain: wait (bounded) until the last load issued into each stage has
-        // landed, so no copy into this CTA's shared memory outlives it.
+      if ((!ok || *abort_flag) && rank == 0) {
+        // Drain: wait (bounded) until the last loads issued into each stage
+        // (by both CTAs of a pair: they signal this CTA's barriers) have
+        // landed, so no copy into shared memory outlives the kernel.
         const uint64_t t0 = globaltimer();
         for (int s = 0; s < STAGES; ++s) {
           if (last_phase[s] < 0) continue;
@@ -343,11 +443,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer ---
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       const uint32_t fmt = p.in_half ? 0u : 1u;  // kind::f16 operand format: 0 = f16, 1 = bf16
       const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(!p.a_kmajor) << 15) |
                              (static_cast<uint32_t>(!p.b_kmajor) << 16) | (static_cast<uint32_t>(BN >> 3) << 17) |
-                             (static_cast<uint32_t>(BM >> 4) << 24);
+                             (static_cast<uint32_t>(G::TILE_M >> 4) << 24);
       const uint32_t a_lbo = p.a_kmajor ? 16u : 8192u;
       const uint32_t b_lbo = p.b_kmajor ? 16u : 8192u;
       const uint32_t a_kstep = p.a_kmajor ? 32u : 2048u;
@@ -356,7 +456,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = unit; t < p.total_tiles && ok; t += nunits, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) { ok = false; break; }
@@ -371,16 +471,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = make_desc(a_addr + kk * a_kstep, a_lbo, 1024u);
             const uint64_t bd = make_desc(b_addr + kk * b_kstep, b_lbo, 1024u);
-            mma_bf16(tmem_d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            if (PAIR == 2) mma_bf16_pair(tmem_d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else mma_bf16(tmem_d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(&empty_bar[stage]);  // frees the stage once these MMAs retire
+          // frees the stage (in every CTA of the pair) once these MMAs retire
+          if (PAIR == 2) mma_commit_pair_both(&empty_bar[stage]);
+          else mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit(&tfull_bar[acc]);      // accumulator ready for the epilogue
+        // accumulator ready for the epilogue warps of every CTA of the pair
+        if (PAIR == 2) mma_commit_pair_both(&tfull_bar[acc]);
+        else mma_commit(&tfull_bar[acc]);
       }
       // Make sure every MMA this thread issued has retired before TMEM is freed.
-      mma_commit(drain_bar);
+      if (PAIR == 2) mma_commit_pair_local(drain_bar);
+      else mma_commit(drain_bar);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(drain_bar, 0)) {
         if (globaltimer() - t0 > kTimeoutNs) { *abort_flag = 1; break; }
@@ -396,19 +502,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     // and symmetrise the diagonal chunk in shared memory before one store.
     const int quad = warp & 3;
     const uint32_t st_base = smem_u32(epi_smem) + static_cast<uint32_t>(warp - 2) * EPI_WARP_BYTES;
+    const uint32_t tempty0 = PAIR == 2 ? map_to_rank(smem_u32(&tempty_bar[0]), 0) : 0u;
+    const uint32_t tempty1 = PAIR == 2 ? map_to_rank(smem_u32(&tempty_bar[1]), 0) : 0u;
     int local = 0;
     const Epilogue& e = p.e;
     const bool vec_c = e.C && ((e.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.C) & 15) == 0) &&
                        ((e.strideC & 7) == 0);
     constexpr bool want_rsq = RSQ != 0;
-    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++local) {
+    for (int t = unit; t < p.total_tiles; t += nunits, ++local) {
       int b, tm, tn;
       tile_coords(p, t, b, tm, tn);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag)) break;
       fence_after_sync();
-      const int r0 = tm * BM + quad * 32;
+      const int r0 = tm * G::TILE_M + static_cast<int>(rank) * BM + quad * 32;
       const int row = r0 + lane;
       const float sc = e.scale ? e.alpha * e.scale[b] : e.alpha;
       const uint16_t* Cb = e.C ? e.C + static_cast<int64_t>(b) * e.strideC : nullptr;
@@ -501,7 +609,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         ch = nch;
       }
       fence_before_sync();
-      mbar_arrive(&tempty_bar[acc]);
+      if (PAIR == 2) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+      else mbar_arrive(&tempty_bar[acc]);
       if (want_rsq && row < p.M)
         e.rowsq[(static_cast<int64_t>(b) * p.tiles_n + tn) * p.M + row] = rsq;
     }
@@ -511,13 +620,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   fence_before_sync();
   __syncthreads();
+  if (PAIR == 2) cluster_sync();  // the pair's MMAs, loads and remote arrivals are finished
   if (threadIdx.x == 0 && *abort_flag) atomicOr(p.err, kErrWaitTimeout);
   (void)DHALF;
   if (warp == 1) {
     __syncwarp();
     fence_after_sync();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
-                 : "memory");
+    if (PAIR == 2)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                   : "memory");
   }
 }
 
@@ -659,15 +773,18 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   }
   if (!gemm_tc_supported(A, B, E, M, N, K)) return gemm_simt(A, B, E, M, N, K, batch, stream);
 
+  // A CTA pair (256-row tiles) once there are rows for both CTAs.
+  const int pair = (M >= 256) ? 2 : 1;
   tc::Params p;
   memset(&p, 0, sizeof(p));
   p.M = M; p.N = N; p.K = K; p.batch = batch;
+  p.tile_m = tc::BM * pair;
   p.a_kmajor = A.kmajor; p.b_kmajor = B.kmajor; p.sym = sym; p.in_half = A.half;
-  p.tiles_m = (M + tc::BM - 1) / tc::BM;
+  p.tiles_m = (M + p.tile_m - 1) / p.tile_m;
   p.tiles_n = (N + tc::BN - 1) / tc::BN;
   if (sym) {
     int cnt = 0;
-    for (int tn = 0; tn < p.tiles_n; ++tn) cnt += std::min(p.tiles_m, (tn * tc::BN + tc::BN - 1) / tc::BM + 1);
+    for (int tn = 0; tn < p.tiles_n; ++tn) cnt += std::min(p.tiles_m, (tn * tc::BN + tc::BN - 1) / p.tile_m + 1);
     p.tiles_per_batch = cnt;
   } else {
     p.tiles_per_batch = p.tiles_m * p.tiles_n;
@@ -679,25 +796,29 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   p.e = E;
   p.err = device_error_word();
   if (!p.err) { set_error("gemm: no device error word"); return -1; }
+  // rowsq partials are laid out per 256-column tile of the output
+  if (E.rowsq && p.tiles_n != (N + 255) / 256) { set_error("gemm: row-sum layout"); return -1; }
 
   CUtensorMap ma, mb, md;
   if (tc::make_map(&ma, A, M, K, batch, tc::BM)) return -1;
-  if (tc::make_map(&mb, B, N, K, batch, tc::BN)) return -1;
+  if (tc::make_map(&mb, B, N, K, batch, tc::BN / pair)) return -1;
   if (tc::make_store_map(&md, E, M, N, batch)) return -1;
 
   using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const tc::Params);
-  // [kind][d_half][sym][rowsq]; invalid combinations are rejected above
-  static const KernelFn table[4][2][2][2] = {
-      {{{tc::gemm_tc_kernel<0, 0, 0, 0>, tc::gemm_tc_kernel<0, 0, 0, 1>}, {tc::gemm_tc_kernel<0, 0, 1, 0>, nullptr}},
-       {{tc::gemm_tc_kernel<0, 1, 0, 0>, tc::gemm_tc_kernel<0, 1, 0, 1>}, {tc::gemm_tc_kernel<0, 1, 1, 0>, nullptr}}},
-      {{{tc::gemm_tc_kernel<1, 0, 0, 0>, tc::gemm_tc_kernel<1, 0, 0, 1>}, {tc::gemm_tc_kernel<1, 0, 1, 0>, nullptr}},
-       {{tc::gemm_tc_kernel<1, 1, 0, 0>, tc::gemm_tc_kernel<1, 1, 0, 1>}, {tc::gemm_tc_kernel<1, 1, 1, 0>, nullptr}}},
-      {{{tc::gemm_tc_kernel<2, 0, 0, 0>, tc::gemm_tc_kernel<2, 0, 0, 1>}, {tc::gemm_tc_kernel<2, 0, 1, 0>, nullptr}},
-       {{nullptr, nullptr}, {nullptr, nullptr}}},
-      {{{tc::gemm_tc_kernel<3, 0, 0, 0>, tc::gemm_tc_kernel<3, 0, 0, 1>}, {tc::gemm_tc_kernel<3, 0, 1, 0>, nullptr}},
-       {{nullptr, nullptr}, {nullptr, nullptr}}},
+#define B2O_K(K_, H_, S_, R_) {tc::gemm_tc_kernel<K_, H_, S_, R_, 1>, tc::gemm_tc_kernel<K_, H_, S_, R_, 2>}
+  // [kind][d_half][sym][rowsq][pair-1]; invalid combinations are rejected above
+  static const KernelFn table[4][2][2][2][2] = {
+      {{{B2O_K(0, 0, 0, 0), B2O_K(0, 0, 0, 1)}, {B2O_K(0, 0, 1, 0), {nullptr, nullptr}}},
+       {{B2O_K(0, 1, 0, 0), B2O_K(0, 1, 0, 1)}, {B2O_K(0, 1, 1, 0), {nullptr, nullptr}}}},
+      {{{B2O_K(1, 0, 0, 0), B2O_K(1, 0, 0, 1)}, {B2O_K(1, 0, 1, 0), {nullptr, nullptr}}},
+       {{B2O_K(1, 1, 0, 0), B2O_K(1, 1, 0, 1)}, {B2O_K(1, 1, 1, 0), {nullptr, nullptr}}}},
+      {{{B2O_K(2, 0, 0, 0), B2O_K(2, 0, 0, 1)}, {B2O_K(2, 0, 1, 0), {nullptr, nullptr}}},
+       {{{nullptr, nullptr}, {nullptr, nullptr}}, {{nullptr, nullptr}, {nullptr, nullptr}}}},
+      {{{B2O_K(3, 0, 0, 0), B2O_K(3, 0, 0, 1)}, {B2O_K(3, 0, 1, 0), {nullptr, nullptr}}},
+       {{{nullptr, nullptr}, {nullptr, nullptr}}, {{nullptr, nullptr}, {nullptr, nullptr}}}},
   };
-  const KernelFn fn = table[E.kind][E.d_half ? 1 : 0][sym ? 1 : 0][E.rowsq ? 1 : 0];
+#undef B2O_K
+  const KernelFn fn = table[E.kind][E.d_half ? 1 : 0][sym ? 1 : 0][E.rowsq ? 1 : 0][pair - 1];
   if (!fn) { set_error("gemm: unsupported epilogue combination"); return -1; }
   static std::mutex attr_mu;
   static std::vector<std::pair<int, const void*>> configured;
@@ -713,8 +834,22 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
       configured.push_back(key);
     }
   }
-  const int grid = std::min(p.total_tiles, num_sms());
-  fn<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, md, p);
+  const int units = std::min(p.total_tiles, num_sms() / pair);
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(units * pair, 1, 1);
+  cfg.blockDim = dim3(tc::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pair;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, fn, ma, mb, md, p);
+  if (le != cudaSuccess) { set_error(std::string("gemm_tc launch: ") + cudaGetErrorString(le)); return le; }
   count_launch();
   return check_launch("gemm_tc");
 }
