@@ -68,7 +68,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -77,7 +77,11 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self):
+        """Start of the timed region (samples before it are warm-up)."""
+        self.t0 = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -89,7 +93,12 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0 = getattr(self, "t0", 0.0)
+        timed = [ln for t, ln in self.lines if t >= t0]
+        window = "timed region"
+        if len(timed) < 2:  # very short timed region: include the warm-up samples
+            timed, window = [ln for _, ln in self.lines], "warm-up + timed region"
+        for ln in timed:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -102,7 +111,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 def gram_flops(m, n, T=5, resets=(2,), mode="gram"):
@@ -244,9 +253,12 @@ def engine_arm(args, world, rank, local):
     _lib.load()
     model = synth.SyntheticLM(cfg, device=dev, seed=0)
     named = list(model.named_parameters())
-    # gradients live in one flat buffer so the end-to-end leg copies them in with one H2D copy
+    # gradients live in one flat buffer so the end-to-end leg copies them in with
+    # one H2D copy; each view starts on a 256-byte boundary, as separately
+    # allocated gradients do
     total = sum(p.numel() for _, p in named)
-    flat_grad = torch.empty(total, dtype=cfg.dtype, device=dev)
+    pad = lambda n: (n + 127) // 128 * 128  # noqa: E731
+    flat_grad = torch.empty(sum(pad(p.numel()) for _, p in named), dtype=cfg.dtype, device=dev)
     grads = synth.make_grads(model, 0, seed=0)
     off = 0
     for (_, p), g in zip(named, grads):
@@ -254,7 +266,7 @@ def engine_arm(args, world, rank, local):
         view = flat_grad[off:off + n].view_as(p)
         view.copy_(g)
         p.grad = view
-        off += n
+        off += pad(n)
     del grads
     muon, adamw = build_optimizers(model, orthogonalizer=args.orthogonalizer, coefficients=args.coefficients,
                                    adam_master="bf16_mt", **RECIPE)
@@ -282,14 +294,17 @@ def engine_arm(args, world, rank, local):
         if sharded is not None:
             sharded.gather()
 
+    sampler = ClockSampler(local)
+    sampler.start()  # samples from the warm-up on, so short timed regions still get clock readings
     for it in range(args.warmup):
         one_step(it)
     torch.cuda.synchronize()
     ortho_events.clear()
     barrier(world)
     torch.cuda.synchronize()
-    sampler = ClockSampler(local)
-    sampler.start()
+    sampler.mark()
+    _lib.gemm_timing(True)
+    _lib.gemm_timing_read()  # discard anything recorded before the timed region
     launches0 = _lib.launch_count()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -299,6 +314,8 @@ def engine_arm(args, world, rank, local):
     end.record(stream)
     torch.cuda.synchronize()
     launches = _lib.launch_count() - launches0
+    gemm_ms, gemm_flops, gemm_n = _lib.gemm_timing_read()
+    _lib.gemm_timing(False)
     clocks = sampler.stop()
     err = _lib.device_error()
     if err:
@@ -310,7 +327,10 @@ def engine_arm(args, world, rank, local):
     mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
     flops = step_flops(model, muon, mode)
     peak_tf, peak_gbs, peak_kind = peaks()
-    achieved = flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None
+    # dominant kernel: the tensor-core GEMM, timed per launch with CUDA events
+    # on its stream inside the timed region; FLOPs are each launch's algorithmic
+    # count (symmetric outputs at half)
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     # AdamW+EMA streaming bytes: p 2+2, rem 2+2, g 2, m 4+4, v 4+4, fp32 EMA 4+4 = 34 B/elem
     adam_elems = sum(p.numel() for g in adamw.param_groups for p in g["params"])
     adam_bytes = adam_elems * 34 / (world if sharded else 1)
@@ -331,11 +351,15 @@ def engine_arm(args, world, rank, local):
         "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
                       "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
         "adamw_gbs": adam_bytes / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else None,
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (Gram Newton-Schulz GEMM list)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (every tensor-core GEMM of the step)",
                      "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": (achieved / peak_tf) if achieved else None,
-                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP, "flops_per_step": flops,
+                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP,
+                     "launches_per_step": gemm_n / args.steps, "gemm_ms_per_step": gemm_ms / args.steps,
+                     "flops_per_launch": gemm_flops / max(1, gemm_n),
                      "peak_kind": f"{peak_kind} bf16 burst"},
+        "orthogonalizer": {"ms_per_step": ortho_ms, "flops_per_step": flops,
+                           "tflops": flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None},
         "clocks": clocks, "gpu_launches": launches,
     }
     if e2e:
@@ -463,7 +487,7 @@ def micro_adamw(args, dev):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--device", choices=["cuda", "cpu"], default=None,

@@ -4,6 +4,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <vector>
+
 #include "../../include/b2o.h"
 
 namespace b2o {
@@ -52,6 +55,17 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
 int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K, int batch,
               cudaStream_t stream);
 bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K);
+
+struct GemmTimer {
+  static GemmTimer& instance();
+  void before(cudaStream_t st, double flops);
+  void after(cudaStream_t st);
+  int read(double* ms, double* flops, int64_t* launches);
+  bool enabled = false;
+  struct Pair { cudaEvent_t a, b; double flops; };
+  std::vector<Pair> pending;
+  std::mutex mu;
+};
 
 // ---- ortho.cu
 struct OrthoGroup {

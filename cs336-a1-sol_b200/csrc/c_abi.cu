@@ -77,6 +77,15 @@ int64_t b2o_launch_count(void) { return g_launches.load(); }
 
 int b2o_num_sms(void) { return num_sms(); }
 
+int b2o_gemm_timing(int enable) {
+  GemmTimer::instance().enabled = enable != 0;
+  return 0;
+}
+
+int b2o_gemm_timing_read(double* ms, double* flops, int64_t* launches) {
+  return GemmTimer::instance().read(ms, flops, launches);
+}
+
 int b2o_check_device_error(void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaStreamSynchronize(st);

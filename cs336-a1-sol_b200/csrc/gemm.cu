@@ -751,6 +751,45 @@ int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int 
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Optional CUDA-event timing of every tensor-core GEMM launch (off by default):
+// the benchmark reads the summed device time and the algorithmic FLOPs of the
+// launches (symmetric outputs counted at half).
+GemmTimer& GemmTimer::instance() {
+  static GemmTimer t;
+  return t;
+}
+void GemmTimer::before(cudaStream_t st, double flops) {
+  if (!enabled) return;
+  std::lock_guard<std::mutex> lk(mu);
+  cudaEvent_t a, b;
+  if (cudaEventCreate(&a) != cudaSuccess) return;
+  if (cudaEventCreate(&b) != cudaSuccess) { cudaEventDestroy(a); return; }
+  cudaEventRecord(a, st);
+  pending.push_back({a, b, flops});
+}
+void GemmTimer::after(cudaStream_t st) {
+  if (!enabled) return;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!pending.empty()) cudaEventRecord(pending.back().b, st);
+}
+int GemmTimer::read(double* ms, double* flops, int64_t* launches) {
+  std::lock_guard<std::mutex> lk(mu);
+  double t = 0.0, f = 0.0;
+  for (auto& e : pending) {
+    cudaEventSynchronize(e.b);
+    float x = 0.f;
+    if (cudaEventElapsedTime(&x, e.a, e.b) == cudaSuccess) t += x;
+    f += e.flops;
+    cudaEventDestroy(e.a);
+    cudaEventDestroy(e.b);
+  }
+  if (ms) *ms = t;
+  if (flops) *flops = f;
+  if (launches) *launches = static_cast<int64_t>(pending.size());
+  pending.clear();
+  return 0;
+}
+
 bool gemm_tc_supported(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, int K) {
   if (M < tc::BM || N < 128 || K < tc::BK) return false;
   if (!al16(A.ptr) || !al16(B.ptr)) return false;
@@ -848,7 +887,9 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  GemmTimer::instance().before(stream, 2.0 * M * N * K * batch * (sym ? 0.5 : 1.0));
   cudaError_t le = cudaLaunchKernelEx(&cfg, fn, ma, mb, md, p);
+  GemmTimer::instance().after(stream);
   if (le != cudaSuccess) { set_error(std::string("gemm_tc launch: ") + cudaGetErrorString(le)); return le; }
   count_launch();
   return check_launch("gemm_tc");

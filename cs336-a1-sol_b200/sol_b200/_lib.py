@@ -71,6 +71,8 @@ SIGNATURES = {
     "b2o_launch_count": (c_int64, []),
     "b2o_check_device_error": (c_int, [c_void_p]),
     "b2o_num_sms": (c_int, []),
+    "b2o_gemm_timing": (c_int, [c_int]),
+    "b2o_gemm_timing_read": (c_int, [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(c_int64)]),
     "b2o_adamw_step": (c_int, [C.POINTER(AdamwTensor), c_int, C.POINTER(AdamwGroup), c_int, c_int, c_int,
                                c_float, c_void_p]),
     "b2o_ema_update": (c_int, [C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_int64), c_int, c_int,
@@ -167,3 +169,14 @@ def device_error(stream: int | None = None) -> int:
     """Synchronises the stream and returns/clears the device error word."""
     lib = load()
     return int(lib.b2o_check_device_error(stream if stream is not None else stream_ptr()))
+
+
+def gemm_timing(enable: bool) -> None:
+    load().b2o_gemm_timing(1 if enable else 0)
+
+
+def gemm_timing_read():
+    """(device ms, algorithmic FLOPs, launches) of the tensor-core GEMM launches since the last read."""
+    ms, fl, n = C.c_double(), C.c_double(), c_int64()
+    load().b2o_gemm_timing_read(C.byref(ms), C.byref(fl), C.byref(n))
+    return ms.value, fl.value, n.value

@@ -45,6 +45,13 @@ int64_t b2o_launch_count(void);
 int b2o_check_device_error(void* stream);
 /* Number of SMs of the current device (used by the host layer for grid sizing). */
 int b2o_num_sms(void);
+/* Measurement hooks (no reference counterpart): when enabled, every
+ * tensor-core GEMM launch is bracketed by CUDA events on its stream;
+ * b2o_gemm_timing_read synchronises on them and returns the summed device
+ * time, the launches' algorithmic FLOPs (symmetric outputs at half) and the
+ * number of launches since the previous read. */
+int b2o_gemm_timing(int enable);
+int b2o_gemm_timing_read(double* ms, double* flops, int64_t* launches);
 
 /* ------------------------------------------------------------------------ *
  * Fused AdamW (+ optional EMA) over a list of tensors.
