@@ -281,6 +281,9 @@ def engine_arm(args, world, rank, local):
         mom = 0.85 + 0.10 * min(1.0, it / MOM_WARMUP)
         for g in muon.param_groups:
             g["momentum"] = mom
+        if sharded is not None:
+            sharded.step()  # AdamW, table gathers overlapped with NorMuon, EMA, arena gather
+            return
         muon.step()
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
@@ -291,8 +294,6 @@ def engine_arm(args, world, rank, local):
             e1.record(stream)
             adam_ev.append((e0, e1))
         ema.update()
-        if sharded is not None:
-            sharded.gather()
 
     sampler = ClockSampler(local)
     sampler.start()  # samples from the warm-up on, so short timed regions still get clock readings

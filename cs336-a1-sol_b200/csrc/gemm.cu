@@ -1,11 +1,12 @@
-// Batched bf16 GEMM for the Newton-Schulz orthogonaliser, written for sm_100a:
-//   * tcgen05.mma (cta_group::1, kind::f16, M=128 N=256 K=16) accumulating fp32
-//     in tensor memory, two 256-column accumulators so the epilogue of one tile
-//     overlaps the main loop of the next;
-//   * operands staged by TMA (cp.async.bulk.tensor, 128-byte swizzle, no
-//     multicast) through a 4-stage mbarrier ring; either operand may be K-major
-//     or MN-major, so tall matrices are consumed in their stored layout;
-//   * a persistent grid (one CTA per SM) walking a static tile schedule;
+// Batched 16-bit GEMM for the Newton-Schulz orthogonaliser, written for sm_100a:
+//   * tcgen05.mma kind::f16 (bf16 or binary16 operands) accumulating fp32 in
+//     tensor memory, two 256-column accumulators so the epilogue of one tile
+//     overlaps the main loop of the next; 128 x 256 tiles on one CTA
+//     (cta_group::1) or 256 x 256 tiles on a CTA pair (cta_group::2);
+//   * operands staged by TMA (cp.async.bulk.tensor, 128-byte swizzle; every
+//     CTA loads its own tiles) through an mbarrier ring; either operand may be
+//     K-major or MN-major, so tall matrices are consumed in their stored layout;
+//   * a persistent grid (one CTA or CTA pair per SM slot) walking a static tile schedule;
 //     symmetric outputs compute only tiles that touch the upper triangle and
 //     mirror them in the epilogue;
 //   * warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (and TMEM owner),

@@ -87,18 +87,46 @@ class ShardedStep:
                     skip.add(i)
             ema._skip = skip
 
+    def _gather_tables(self, async_op=False):
+        works = []
+        for p in self.row_sharded:
+            flat = p.data.view(-1)
+            per = flat.numel() // self.world
+            w = dist.all_gather_into_tensor(flat, flat[self.rank * per:(self.rank + 1) * per], group=self.group,
+                                            async_op=async_op)
+            if async_op:
+                works.append(w)
+        return works
+
+    def _gather_arena(self, async_op=False):
+        if not self.chunk:
+            return None
+        mine = self.arena[self.rank * self.chunk:(self.rank + 1) * self.chunk]
+        return dist.all_gather_into_tensor(self.arena, mine, group=self.group, async_op=async_op)
+
     @torch.no_grad()
     def gather(self):
         """All-gathers the updated bf16 weights (in place)."""
         if self.world == 1:
             return
-        if self.chunk:
-            mine = self.arena[self.rank * self.chunk:(self.rank + 1) * self.chunk]
-            dist.all_gather_into_tensor(self.arena, mine, group=self.group)
-        for p in self.row_sharded:
-            flat = p.data.view(-1)
-            per = flat.numel() // self.world
-            dist.all_gather_into_tensor(flat, flat[self.rank * per:(self.rank + 1) * per], group=self.group)
+        self._gather_arena()
+        self._gather_tables()
+
+    @torch.no_grad()
+    def step(self):
+        """One sharded optimizer step: AdamW first, so the all-gathers of the
+        vocabulary tables run on NCCL's stream while NorMuon computes; then
+        NorMuon, the EMA update and the all-gather of the NorMuon arena.
+        Same results as muon.step(); adamw.step(); ema.update(); gather()."""
+        self.adamw.step()
+        works = self._gather_tables(async_op=True) if self.world > 1 else []
+        self.muon.step()
+        if self.ema is not None:
+            self.ema.update()
+        if self.world > 1:
+            self._gather_arena()
+        for w in works:
+            w.wait()
 
     @torch.no_grad()
     def gather_ema(self):

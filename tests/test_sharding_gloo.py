@@ -1,0 +1,130 @@
+"""Multi-rank plumbing of the sharded step on CPU ranks (gloo): partition,
+in-place all-gather of the NorMuon arena and of row-sharded tables, EMA
+gather, and failure detection when a rank leaves. The per-rank compute is the
+GPU engine (covered by the GPU tests); here each rank writes a known pattern
+into the parameters it owns."""
+import datetime
+import os
+import socket
+import zlib
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from sol_b200 import EmaWeights, build_optimizers, synth
+from sol_b200.sharding import ShardedStep, assign_matrices, gram_cost
+
+KW = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_partition_is_balanced_and_deterministic(world):
+    model = synth.SyntheticLM(synth.C2, device="meta")
+    from sol_b200.routing import route_params
+    mats = route_params(model.named_parameters())[0]
+    shapes = [tuple(p.shape) for p in mats]
+    owner, load = assign_matrices(shapes, world)
+    assert owner == assign_matrices(shapes, world)[0]
+    assert sorted(set(owner)) == list(range(world))
+    total = sum(gram_cost(s) for s in shapes)
+    biggest = max(gram_cost(s) for s in shapes)
+    assert max(load) <= total / world + biggest  # LPT bound
+
+
+def _expected(name, shape, dtype):
+    g = torch.Generator().manual_seed(zlib.crc32(name.encode()))
+    return torch.randn(shape, generator=g).to(dtype)
+
+
+def _worker(rank, world, port, mode, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+        model = synth.SyntheticLM(synth.MICRO, seed=0)
+        muon, adamw = build_optimizers(model, **KW)
+        ema = EmaWeights(model, 0.999)
+        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16)
+        named = list(model.named_parameters())
+        # "step": each rank writes the final values of what it owns
+        with torch.no_grad():
+            for n, p in named:
+                full = _expected(n, p.shape, p.dtype)
+                if id(p) in sharded.owner:
+                    if sharded.owner[id(p)] == rank:
+                        p.copy_(full)
+                    else:
+                        p.zero_()
+                elif any(p is t for t in sharded.row_sharded):
+                    start, cnt = adamw._owned_slices[id(p)]
+                    p.zero_()
+                    p.view(-1)[start:start + cnt].copy_(full.view(-1)[start:start + cnt])
+                else:
+                    p.copy_(full)  # replicated: every rank computes it
+        if mode == "leave" and rank == world - 1:
+            q.put((rank, "left"))
+            return  # leaves between steps, before the exchange
+        try:
+            sharded.gather()
+        except Exception as e:  # noqa: BLE001
+            q.put((rank, "error: " + type(e).__name__))
+            return
+        bad = [n for n, p in named if not torch.equal(p.data, _expected(n, p.shape, p.dtype))]
+        # EMA shadows: owners set a pattern, gather_ema completes the others
+        with torch.no_grad():
+            for i, (n, p) in enumerate(named):
+                if i not in ema._skip:
+                    ema.shadow[i].copy_(_expected(n, p.shape, torch.float32))
+        sharded.gather_ema()
+        bad_ema = [n for i, (n, p) in enumerate(named)
+                   if not torch.equal(ema.shadow[i], _expected(n, p.shape, torch.float32))]
+        q.put((rank, {"bad": bad, "bad_ema": bad_ema, "owned": len(muon._owned)}))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    for _ in range(world):
+        r, v = q.get(timeout=120)
+        out[r] = v
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_reassembles_every_parameter(world):
+    out = _run(world, "ok")
+    assert sorted(out) == list(range(world))
+    for r, v in out.items():
+        assert v["bad"] == [], (r, v["bad"])
+        assert v["bad_ema"] == [], (r, v["bad_ema"])
+    assert sum(v["owned"] for v in out.values()) == 3 * 5  # MICRO: 3 layers x 5 NorMuon matrices
+
+
+def test_rank_leaving_is_detected_not_hung():
+    """A rank that leaves before the exchange makes the others' gather fail
+    within the process-group timeout instead of hanging."""
+    out = _run(2, "leave")
+    assert out[1] == "left"
+    assert isinstance(out[0], str) and out[0].startswith("error"), out[0]
