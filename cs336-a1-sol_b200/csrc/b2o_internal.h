@@ -28,6 +28,11 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
                   uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
                   float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
                   float w_beta2, float ema_weight, float* scratch, cudaStream_t stream);
+int64_t normuon_apply_static_max_floats();
+int normuon_apply_static(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
+                         uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
+                         float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
+                         float w_beta2, float ema_weight, cudaStream_t stream);
 
 // ---- gemm.cu
 // Operand view: element (row i, k) of an op(A) that is M x K (or op(B) that is N x K).

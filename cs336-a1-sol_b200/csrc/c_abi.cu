@@ -172,6 +172,17 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
                        static_cast<cudaStream_t>(stream));
 }
 
+int64_t b2o_normuon_apply_static_max_floats(void) { return normuon_apply_static_max_floats(); }
+
+int b2o_normuon_apply_static(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c, void* const* params,
+                             uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
+                             float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
+                             float w_beta2, float ema_weight, void* stream) {
+  return normuon_apply_static(d_o, d_rowsq, S, r, c, params, rems, emas, vrows, param_dtype, neg_lr, lr_wd,
+                              wd_factor, wd_on, cautious, shape_scale, w_beta2, ema_weight,
+                              static_cast<cudaStream_t>(stream));
+}
+
 int b2o_gemm(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_kmajor, const uint16_t* d_B, int64_t ldb,
              int64_t strideB, int b_kmajor, uint16_t* d_D, int64_t ldd, int64_t strideD, const uint16_t* d_C,
              int64_t ldc, int64_t strideC, int M, int N, int K, int batch, int in_dtype, int out_dtype, int epi, int sym,

@@ -11,6 +11,8 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
+#include <string>
 #include <vector>
 
 namespace b2o {
@@ -645,6 +647,59 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
     normuon_apply_kernel<2><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
   count_launch();
   return check_launch("normuon_apply");
+}
+
+// ----------------------------------------------- allocation-free variant ---
+// Scratch of b2o_normuon_apply_static: file-scope device memory, reserved by
+// every GPU that loads the library (1 MiB each) for the life of the process.
+// Its address is taken once per device with cudaGetSymbolAddress (the array's
+// name in host code is only a stand-in for the symbol, never a device address).
+constexpr int64_t kStaticApplyScratchFloats = int64_t(1) << 18;
+static __device__ __align__(256) float g_static_apply_scratch[kStaticApplyScratchFloats];
+
+constexpr int kStaticMaxDevices = 64;
+static float* g_static_scratch_ptr[kStaticMaxDevices];
+static std::mutex g_static_scratch_mu;
+
+int64_t normuon_apply_static_max_floats() { return kStaticApplyScratchFloats; }
+
+int normuon_apply_static(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
+                         uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
+                         float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
+                         float w_beta2, float ema_weight, cudaStream_t stream) {
+  if (S <= 0 || r <= 0) { set_error("normuon_apply_static: bad args"); return -1; }
+  const int64_t need = static_cast<int64_t>(S) * (r + 4);
+  if (need > kStaticApplyScratchFloats) {
+    set_error("normuon_apply_static: needs " + std::to_string(need) + " scratch floats (S*(r+4)); the static " +
+              "scratch holds " + std::to_string(kStaticApplyScratchFloats) + "; split the batch or use " +
+              "b2o_normuon_apply with caller scratch");
+    return -1;
+  }
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) {
+    set_error(std::string("normuon_apply_static: no usable current device: ") + cudaGetErrorString(e));
+    return -1;
+  }
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+    if (!g_static_scratch_ptr[dev]) {
+      // set-up on the first call on this device, with the device current
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_static_apply_scratch);
+      if (e != cudaSuccess || !ptr) {
+        set_error(std::string("normuon_apply_static: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+        return -1;
+      }
+      g_static_scratch_ptr[dev] = static_cast<float*>(ptr);
+    }
+    scratch = g_static_scratch_ptr[dev];
+  }
+  // The finish kernel writes every scratch float that the apply kernel reads
+  // (per-row factors and the per-matrix factor), so nothing needs clearing.
+  return normuon_apply(O, rowsq, S, r, c, params, rems, emas, vrows, param_dtype, neg_lr, lr_wd, wd_factor, wd_on,
+                       cautious, shape_scale, w_beta2, ema_weight, scratch, stream);
 }
 
 }  // namespace b2o

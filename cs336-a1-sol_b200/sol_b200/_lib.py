@@ -93,6 +93,11 @@ SIGNATURES = {
     "b2o_normuon_apply": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, C.POINTER(c_void_p),
                                   C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_void_p), c_int, c_float,
                                   c_float, c_float, c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p]),
+    "b2o_normuon_apply_static_max_floats": (c_int64, []),
+    "b2o_normuon_apply_static": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, C.POINTER(c_void_p),
+                                         C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_void_p), c_int,
+                                         c_float, c_float, c_float, c_int, c_int, c_float, c_float, c_float,
+                                         c_void_p]),
     "b2o_gemm_bf16": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int, c_void_p,
                               c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                               c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),

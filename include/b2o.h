@@ -169,6 +169,28 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
                       float shape_scale, float w_beta2, float ema_weight,
                       float* d_scratch, void* stream);
 
+/* Allocation-free form of b2o_normuon_apply. No counterpart in the reference
+ * (its optimizer allocates its temporaries through PyTorch).
+ * For hosts that cannot hand the library a scratch buffer: a caller whose
+ * device memory is entirely reserved up front by another allocator, or a
+ * runtime that forbids allocating while its step is in flight. The
+ * S * (r + 4) floats of scratch come from a 1 MiB array inside the library
+ * (b2o_normuon_apply_static_max_floats() = 262144 floats); larger batches are
+ * rejected with a negative status and a message, nothing launched. The library
+ * allocates nothing: the first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, once per device, with that device current),
+ * so make that first call before any stream capture. All calls share the one
+ * array per device: two calls whose kernels overlap on the GPU (different
+ * streams, no ordering between them) race on it. Every scratch value the
+ * kernels read is written earlier in the same call, so no clearing is needed.
+ * Arguments and results are those of b2o_normuon_apply without d_scratch. */
+int64_t b2o_normuon_apply_static_max_floats(void);
+int b2o_normuon_apply_static(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c,
+                             void* const* params, uint16_t* const* rems, float* const* emas,
+                             float* const* vrows, int param_dtype,
+                             float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious,
+                             float shape_scale, float w_beta2, float ema_weight, void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Batched bf16 GEMM on tcgen05 (exposed for tests and the micro-benchmark).
  * D[b] = epilogue(op(A[b]) * op(B[b])), fp32 accumulation in tensor memory.
