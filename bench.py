@@ -40,9 +40,10 @@ from sol_b200.sharding import ShardedStep  # noqa: E402
 
 RECIPE = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
 MOM_WARMUP = 300
-# dram__bytes_read.sum + dram__bytes_write.sum of one Gram-NS GEMM launch list,
-# from profiles/ (None until a capture exists for the current kernel).
-GEMM_TRAFFIC_BYTES_PER_STEP = None
+# dram__bytes_read.sum + dram__bytes_write.sum per tensor-core GEMM launch,
+# averaged over the 30 launches of one L14 step (ncu capture summarised in
+# profiles/gemm_tc_c2_L14_dram_traffic.md); only meaningful for the default config.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.179e8
 
 
 def peaks():
@@ -310,8 +311,11 @@ def engine_arm(args, world, rank, local):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
+    host_t = 0.0
     for k in range(args.steps):
+        h0 = time.perf_counter()
         one_step(args.warmup + k, record=True)
+        host_t += time.perf_counter() - h0
     end.record(stream)
     torch.cuda.synchronize()
     launches = _lib.launch_count() - launches0
@@ -355,12 +359,14 @@ def engine_arm(args, world, rank, local):
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (every tensor-core GEMM of the step)",
                      "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": (achieved / peak_tf) if achieved else None,
-                     "traffic": GEMM_TRAFFIC_BYTES_PER_STEP,
+                     "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if (args.config == "c2_L14_d1024" and world == 1)
+                     else None,
                      "launches_per_step": gemm_n / args.steps, "gemm_ms_per_step": gemm_ms / args.steps,
                      "flops_per_launch": gemm_flops / max(1, gemm_n),
                      "peak_kind": f"{peak_kind} bf16 burst"},
         "orthogonalizer": {"ms_per_step": ortho_ms, "flops_per_step": flops,
                            "tflops": flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None},
+        "host_enqueue_ms_per_step": host_t * 1e3 / args.steps,
         "clocks": clocks, "gpu_launches": launches,
     }
     if e2e:
@@ -446,7 +452,7 @@ def micro_adamw(args, dev):
     from sol_b200 import AdamW, EmaWeights
     g = torch.Generator(device=dev).manual_seed(0)
     params = [torch.nn.Parameter((torch.randn(32768, 1024, generator=g, device=dev) * 0.02).to(torch.bfloat16))
-              for _ in range(7)]
+              for _ in range(args.tables)]
     params.append(torch.nn.Parameter(torch.ones(1 << 20, device=dev, dtype=torch.bfloat16)))
     for p in params:
         p.grad = (torch.randn(p.shape, generator=g, device=dev) * 1e-4).to(torch.bfloat16)
@@ -501,6 +507,7 @@ def main():
     ap.add_argument("--micro", choices=["gram", "adamw"], default=None,
                     help="run a BASELINE micro-benchmark (configs[2] / configs[3]) instead of the full step")
     ap.add_argument("--shape", default="1024x1024,3072x1024,5632x1024,1024x5632")
+    ap.add_argument("--tables", type=int, default=7, help="--micro adamw: number of 32768x1024 tables")
     args = ap.parse_args()
     if args.device is None:
         args.device = "cuda" if args.impl == "engine" else "cpu"
