@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 namespace b2o {
 
@@ -46,6 +47,33 @@ __device__ __forceinline__ uint16_t f32_to_f16(float f) { return __half_as_ushor
 // 16-bit storage of either kind: half != 0 selects binary16, else bfloat16.
 __device__ __forceinline__ float h16_to_f32(uint16_t h, int half) { return half ? f16_to_f32(h) : bf16_to_f32(h); }
 __device__ __forceinline__ uint16_t f32_to_h16(float f, int half) { return half ? f32_to_f16(f) : f32_to_bf16(f); }
+
+// ------------------------------------------- programmatic dependent launch ---
+// Every library kernel is launched with programmatic stream serialisation: it
+// lets its dependents launch early (trigger) and waits for its predecessor to
+// complete and flush before touching global memory (wait), so launch latency
+// and the previous kernel's tail overlap.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// B2O_PDL=0 in the environment launches every kernel in plain stream order.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // torch's lerp (ATen/native/Lerp.h): small weights interpolate from `self`,
 // large ones from `end`; evaluated in fp32 opmath with fused multiply-add.

@@ -3,6 +3,7 @@
 #include "b2o_common.cuh"
 #include "b2o_internal.h"
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -14,6 +15,14 @@ std::atomic<int64_t> g_launches{0};
 static thread_local std::string t_last_error;
 
 void set_error(const std::string& msg) { t_last_error = msg; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("B2O_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();

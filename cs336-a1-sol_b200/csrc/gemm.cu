@@ -374,6 +374,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (PAIR == 2) cluster_sync();  // the peer's barriers exist before any remote arrival
   fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // the set-up above overlaps the previous kernel's tail; no global memory is
+  // touched before the previous kernel has completed
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer --
@@ -621,6 +624,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   fence_before_sync();
   __syncthreads();
+  pdl_trigger();  // this CTA's work is done: the next kernel may start launching
   if (PAIR == 2) cluster_sync();  // the pair's MMAs, loads and remote arrivals are finished
   if (threadIdx.x == 0 && *abort_flag) atomicOr(p.err, kErrWaitTimeout);
   (void)DHALF;
@@ -699,6 +703,7 @@ static int make_store_map(CUtensorMap* map, const Epilogue& E, int M, int N, int
 // ------------------------------------------------------------- CUDA cores --
 // One CTA computes a 256-column row segment of one output row.
 __global__ void __launch_bounds__(256) gemm_simt_kernel(Operand A, Operand B, Epilogue E, int M, int N, int K) {
+  pdl_wait();
   const int tn = blockIdx.x, row = blockIdx.y, b = blockIdx.z;
   const int col = tn * 256 + threadIdx.x;
   const uint16_t* Ab = A.ptr + static_cast<int64_t>(b) * A.stride;
@@ -745,7 +750,7 @@ int gemm_simt(const Operand& A, const Operand& B, const Epilogue& E, int M, int 
               cudaStream_t stream) {
   dim3 grid((N + 255) / 256, M, batch);
   if (grid.y > 65535u || grid.z > 65535u) { set_error("gemm_simt: problem too large"); return -1; }
-  gemm_simt_kernel<<<grid, 256, 0, stream>>>(A, B, E, M, N, K);
+  launch_pdl(gemm_simt_kernel, grid, dim3(256), 0, stream, A, B, E, M, N, K);
   count_launch();
   return check_launch("gemm_simt");
 }
@@ -881,13 +886,15 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   cfg.blockDim = dim3(tc::THREADS, 1, 1);
   cfg.dynamicSmemBytes = tc::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = pair;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   GemmTimer::instance().before(stream, 2.0 * M * N * K * batch * (sym ? 0.5 : 1.0));
   cudaError_t le = cudaLaunchKernelEx(&cfg, fn, ma, mb, md, p);
   GemmTimer::instance().after(stream);

@@ -80,6 +80,7 @@ int64_t ortho_workspace_bytes(int S, int r, int c) {
 // this group's matrices start at s_off.
 __global__ void norm_finalize_kernel(const float* __restrict__ partial, int nparts, int S, int mode, float eps,
                                      float safety, float* __restrict__ scal, int Stot, int s_off) {
+  pdl_wait();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= S) return;
   float acc = 0.f;
@@ -99,6 +100,7 @@ __global__ void norm_finalize_kernel(const float* __restrict__ partial, int npar
 // X0 = binary16(u * scale[s]): the normalised Gram-iteration input.
 __global__ void to_half_scaled_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
                                       const float* __restrict__ scale) {
+  pdl_wait();
   const int s = blockIdx.y;
   const float sc = scale[s];
   const uint16_t* u = U + static_cast<int64_t>(s) * rc;
@@ -124,6 +126,7 @@ __global__ void to_half_scaled_kernel(const uint16_t* __restrict__ U, uint16_t* 
 // X0 = bf16(u / d[s]) (the division of zeropower_via_newtonschulz5, sol_modules.py:283).
 __global__ void ns_normalize_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
                                     const float* __restrict__ div) {
+  pdl_wait();
   const int s = blockIdx.y;
   const float d = div[s];
   const uint16_t* u = U + static_cast<int64_t>(s) * rc;
@@ -222,8 +225,8 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
 
   for (int g = 0; g < ng; ++g) {
     const int nparts = normuon_front_parts(bg[g].rc);
-    norm_finalize_kernel<<<(bg[g].S + 127) / 128, 128, 0, stream>>>(groups[g].partial, nparts, bg[g].S, mode,
-                                                                      norm_eps, norm_safety, scal, L.Stot, L.s_off[g]);
+    launch_pdl(norm_finalize_kernel, dim3((bg[g].S + 127) / 128), dim3(128), 0, stream, groups[g].partial, nparts,
+               bg[g].S, mode, norm_eps, norm_safety, scal, L.Stot, L.s_off[g]);
     count_launch();
     if (int e = check_launch("norm_finalize")) return e;
   }
@@ -236,7 +239,8 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
       const int64_t rc = bg[g].rc;
       const int S = bg[g].S;
       const int gx = static_cast<int>(std::min<int64_t>((rc + 255) / 256, std::max(1, num_sms() * 8 / S)));
-      ns_normalize_kernel<<<dim3(gx, S), 256, 0, stream>>>(groups[g].U, xa(g), rc, scal + 2 * L.Stot + L.s_off[g]);
+      launch_pdl(ns_normalize_kernel, dim3(gx, S), dim3(256), 0, stream, groups[g].U, xa(g), rc,
+                 static_cast<const float*>(scal + 2 * L.Stot + L.s_off[g]));
       count_launch();
       if (int e = check_launch("ns_normalize")) return e;
       X[g] = xa(g);
@@ -283,7 +287,8 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     const int64_t rc = bg[g].rc;
     const int S = bg[g].S;
     const int gx = static_cast<int>(std::min<int64_t>((rc / 8 + 255) / 256 + 1, std::max(1, num_sms() * 8 / S)));
-    to_half_scaled_kernel<<<dim3(gx, S), 256, 0, stream>>>(groups[g].U, xa(g), rc, scal + L.s_off[g]);
+    launch_pdl(to_half_scaled_kernel, dim3(gx, S), dim3(256), 0, stream, groups[g].U, xa(g), rc,
+               static_cast<const float*>(scal + L.s_off[g]));
     count_launch();
     if (int e = check_launch("to_half_scaled")) return e;
     Xcur[g] = xa(g);

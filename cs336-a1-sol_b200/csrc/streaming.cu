@@ -115,6 +115,7 @@ __device__ __forceinline__ void adam_elem(const AdamCoef& c, float& w, float gra
 
 template <typename PT, typename ST>
 __global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_constant__ AdamTable tab) {
+  pdl_wait();
   const int total_chunks = tab.chunk_start[tab.ntensors];
   for (int chunk = blockIdx.x; chunk < total_chunks; chunk += gridDim.x) {
     // locate the tensor owning this chunk (<= kAdamMaxTensors entries)
@@ -240,11 +241,11 @@ int adamw_step(const b2o_adamw_tensor* tensors, int ntensors, const b2o_adamw_gr
     if (chunks > 0) {
       const int grid = std::min(chunks, num_sms() * 8);
       if (param_dtype == B2O_F32)
-        adamw_kernel<float, float><<<grid, kAdamThreads, 0, stream>>>(tab);
+        launch_pdl(adamw_kernel<float, float>, dim3(grid), dim3(kAdamThreads), 0, stream, tab);
       else if (state_dtype == B2O_F32)
-        adamw_kernel<uint16_t, float><<<grid, kAdamThreads, 0, stream>>>(tab);
+        launch_pdl(adamw_kernel<uint16_t, float>, dim3(grid), dim3(kAdamThreads), 0, stream, tab);
       else
-        adamw_kernel<uint16_t, uint16_t><<<grid, kAdamThreads, 0, stream>>>(tab);
+        launch_pdl(adamw_kernel<uint16_t, uint16_t>, dim3(grid), dim3(kAdamThreads), 0, stream, tab);
       count_launch();
       if (int e = check_launch("adamw")) return e;
     }
@@ -268,6 +269,7 @@ constexpr int kEmaChunk = 256 * 8 * 4;
 
 template <typename PT, bool TO_PARAM>
 __global__ void __launch_bounds__(256) ema_kernel(const __grid_constant__ EmaTable tab) {
+  pdl_wait();
   const int total = tab.chunk_start[tab.count];
   for (int chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
     int lo = 0, hi = tab.count - 1;
@@ -328,8 +330,8 @@ static int ema_launch(float* const* shadows, const void* const* params, const in
     tab.w = w;
     if (chunks > 0) {
       const int grid = std::min(chunks, num_sms() * 8);
-      if (param_dtype == B2O_F32) ema_kernel<float, TO_PARAM><<<grid, 256, 0, stream>>>(tab);
-      else ema_kernel<uint16_t, TO_PARAM><<<grid, 256, 0, stream>>>(tab);
+      if (param_dtype == B2O_F32) launch_pdl(ema_kernel<float, TO_PARAM>, dim3(grid), dim3(256), 0, stream, tab);
+      else launch_pdl(ema_kernel<uint16_t, TO_PARAM>, dim3(grid), dim3(256), 0, stream, tab);
       count_launch();
       if (int e = check_launch("ema")) return e;
     }
@@ -364,6 +366,7 @@ template <typename T>
 __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(
     const __grid_constant__ FrontTable tab, int64_t rc, int nparts, float w_small, float w_large,
     int nesterov, int vec_ok, uint16_t* __restrict__ U, float* __restrict__ partial) {
+  pdl_wait();
   const int s = blockIdx.y;
   const T* G = reinterpret_cast<const T*>(tab.g[s]);
   T* B = reinterpret_cast<T*>(tab.buf[s]);
@@ -437,11 +440,11 @@ int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int
   const int nparts = normuon_front_parts(rc);
   dim3 grid(nparts, S);
   if (dtype == B2O_F32)
-    normuon_front_kernel<float><<<grid, kFrontThreads, 0, stream>>>(tab, rc, nparts, w_small, w_large,
-                                                                     nesterov, vec_ok, U, partial);
+    launch_pdl(normuon_front_kernel<float>, grid, dim3(kFrontThreads), 0, stream, tab, rc, nparts, w_small,
+               w_large, nesterov, vec_ok, U, partial);
   else
-    normuon_front_kernel<uint16_t><<<grid, kFrontThreads, 0, stream>>>(tab, rc, nparts, w_small, w_large,
-                                                                        nesterov, vec_ok, U, partial);
+    launch_pdl(normuon_front_kernel<uint16_t>, grid, dim3(kFrontThreads), 0, stream, tab, rc, nparts, w_small,
+               w_large, nesterov, vec_ok, U, partial);
   count_launch();
   return check_launch("normuon_front");
 }
@@ -472,6 +475,7 @@ __device__ float block_sum_1024(float x, float* red) {
 __global__ void __launch_bounds__(1024) normuon_finish_kernel(
     const __grid_constant__ VrowTable vt, const float* __restrict__ rowsq, int r, int c, int ntn,
     float w_beta2, float* __restrict__ scratch) {
+  pdl_wait();
   __shared__ float red[33];
   const int s = blockIdx.x;
   float* inv = scratch + static_cast<int64_t>(s) * (r + 4);
@@ -539,6 +543,7 @@ template <int MODE>
 __global__ void __launch_bounds__(256) normuon_apply_kernel(
     const __grid_constant__ ApplyTable tab, const __grid_constant__ ApplyArgs a,
     const uint16_t* __restrict__ O, const float* __restrict__ scratch) {
+  pdl_wait();
   const int s = blockIdx.y;
   const float* inv = scratch + static_cast<int64_t>(s) * (a.r + 4);
   const float f = inv[a.r];
@@ -632,7 +637,7 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
   }
   a.vec_ok = vec_ok;
   const int ntn = (c + 255) / 256;
-  normuon_finish_kernel<<<S, 1024, 0, stream>>>(vt, rowsq, r, c, ntn, w_beta2, scratch);
+  launch_pdl(normuon_finish_kernel, dim3(S), dim3(1024), 0, stream, vt, rowsq, r, c, ntn, w_beta2, scratch);
   count_launch();
   if (int e = check_launch("normuon_finish")) return e;
   const int64_t per_part = 256 * 8 * 4;
@@ -640,11 +645,11 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
   const int gx = std::max(1, std::min(parts, (num_sms() * 8 + S - 1) / S));
   dim3 grid(gx, S);
   if (param_dtype == B2O_F32)
-    normuon_apply_kernel<0><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+    launch_pdl(normuon_apply_kernel<0>, grid, dim3(256), 0, stream, tab, a, O, scratch);
   else if (rems)
-    normuon_apply_kernel<1><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+    launch_pdl(normuon_apply_kernel<1>, grid, dim3(256), 0, stream, tab, a, O, scratch);
   else
-    normuon_apply_kernel<2><<<grid, 256, 0, stream>>>(tab, a, O, scratch);
+    launch_pdl(normuon_apply_kernel<2>, grid, dim3(256), 0, stream, tab, a, O, scratch);
   count_launch();
   return check_launch("normuon_apply");
 }
