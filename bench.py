@@ -262,27 +262,43 @@ def engine_arm(args, world, rank, local):
     flat_grad = torch.empty(sum(pad(p.numel()) for _, p in named), dtype=cfg.dtype, device=dev)
     grads = synth.make_grads(model, 0, seed=0)
     off = 0
+    grad_offsets = []
     for (_, p), g in zip(named, grads):
         n = p.numel()
         view = flat_grad[off:off + n].view_as(p)
         view.copy_(g)
         p.grad = view
+        grad_offsets.append(off)
         off += pad(n)
     del grads
     muon, adamw = build_optimizers(model, orthogonalizer=args.orthogonalizer, coefficients=args.coefficients,
                                    adam_master="bf16_mt", **RECIPE)
     ema = EmaWeights(model, 0.999)
-    sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank) if world > 1 else None
+    sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank,
+                          exchange=args.exchange) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     ortho_events = []
     adam_ev = []
+    shard_marks = []
 
     def one_step(it, record=False):
         mom = 0.85 + 0.10 * min(1.0, it / MOM_WARMUP)
         for g in muon.param_groups:
             g["momentum"] = mom
         if sharded is not None:
-            sharded.step()  # AdamW, table gathers overlapped with NorMuon, EMA, arena gather
+            # AdamW, table gathers overlapped with NorMuon, EMA, arena gather
+            if record:
+                marks = [("start", torch.cuda.Event(enable_timing=True))]
+                marks[0][1].record(stream)
+
+                def mark(name):
+                    ev = torch.cuda.Event(enable_timing=True)
+                    ev.record(stream)
+                    marks.append((name, ev))
+                sharded.step(mark)
+                shard_marks.append(marks)
+            else:
+                sharded.step()
             return
         muon.step()
         if record:
@@ -339,6 +355,12 @@ def engine_arm(args, world, rank, local):
     ms = max_over_ranks(ms_local, world, dev)
     ortho_ms = sum(a.elapsed_time(b) for a, b in ortho_events) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in adam_ev) / args.steps
+    shard_phases = {}
+    for marks in shard_marks:
+        for (_, a), (name, b) in zip(marks, marks[1:]):
+            shard_phases[name] = shard_phases.get(name, 0.0) + a.elapsed_time(b) / args.steps
+    if shard_phases:
+        adam_ms = shard_phases["adamw"]
     mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
     flops = step_flops(model, muon, mode)
     peak_tf, peak_gbs, peak_kind = peaks()
@@ -352,7 +374,7 @@ def engine_arm(args, world, rank, local):
 
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev)
+        e2e = e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev, grad_offsets)
     line = {
         "metric": "optimizer step ms (NorMuon+AdamW+EMA)", "value": ms, "unit": "ms", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
@@ -362,9 +384,11 @@ def engine_arm(args, world, rank, local):
                    "orthogonalizer": f"{args.orthogonalizer}/{args.coefficients if mode == 'gram' else 'quintic'}",
                    "adamw": "bf16 + bf16 remainder, fp32 moments", "ema": "fp32, folded",
                    "l2": "working set > L2 (126 MB); no flush",
-                   "parallelism": f"shard{world}" if world > 1 else "single"},
+                   "parallelism": f"shard{world}" if world > 1 else "single",
+                   "exchange": sharded.exchange if sharded is not None else None},
         "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
                       "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
+        "sharded_phases_ms": shard_phases or None,
         "adamw_gbs": adam_bytes / (adam_ms * 1e-3) / 1e9 if adam_ms > 0 else None,
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (every tensor-core GEMM of the step)",
                      "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
@@ -383,19 +407,48 @@ def engine_arm(args, world, rank, local):
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg)
+    if sharded is not None:
+        sharded.close()
     return line
 
 
-def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev):
+def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev, grad_offsets):
     """Same step through the public API, with the step's gradients copied in
-    from pinned host memory and a result read back every step."""
+    from pinned host memory and a result read back every step. A sharded rank
+    copies in only the gradients its optimizer shard reads (its NorMuon
+    matrices, its rows of the split tables and the small replicated tensors),
+    as a rank does after a gradient reduce-scatter."""
     host = torch.empty(flat_grad.numel(), dtype=flat_grad.dtype, pin_memory=True)
     host.copy_(flat_grad.cpu())
+    ranges = []
+    for (_, p), off in zip(model.named_parameters(), grad_offsets):
+        n = p.numel()
+        if sharded is None:
+            ranges.append((off, n))
+        elif id(p) in sharded.owner:
+            if sharded.owner[id(p)] == sharded.rank:
+                ranges.append((off, n))
+        else:
+            start, cnt = adamw._owned_slices.get(id(p), (0, n))
+            ranges.append((off + start, cnt))
+    merged = []
+    for off, n in sorted(ranges):
+        if merged and merged[-1][0] + merged[-1][1] >= off:
+            o0, n0 = merged[-1]
+            merged[-1] = (o0, max(n0, off + n - o0))
+        else:
+            merged.append((off, n))
+    h2d = sum(n for _, n in merged) * host.element_size()
     probe = next(iter(muon.param_groups[0]["params"]))
     out = torch.empty(256, dtype=probe.dtype, pin_memory=True)
     stream = torch.cuda.current_stream(dev)
+
+    def copy_in():
+        for off, n in merged:
+            flat_grad[off:off + n].copy_(host[off:off + n], non_blocking=True)
+
     for it in range(2):
-        flat_grad.copy_(host, non_blocking=True)
+        copy_in()
         one_step(it)
         out.copy_(probe.detach().reshape(-1)[:256], non_blocking=True)
     torch.cuda.synchronize()
@@ -404,101 +457,14 @@ def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, 
     e = torch.cuda.Event(enable_timing=True)
     s.record(stream)
     for k in range(args.steps):
-        flat_grad.copy_(host, non_blocking=True)
+        copy_in()
         one_step(k)
         out.copy_(probe.detach().reshape(-1)[:256], non_blocking=True)
     e.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / args.steps, world, dev)
-    return {"value": ms, "unit": "ms", "h2d_bytes_per_step": host.numel() * host.element_size(),
+    return {"value": ms, "unit": "ms", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": out.numel() * out.element_size()}
-
-
-# ----------------------------------------------------------- micro legs ---
-def micro_gram(args, dev):
-    """batched orthogonalisation, 14 matrices per shape,
-    5 iterations, N(0,1) inputs scaled to unit spectral norm."""
-    from sol_b200 import NorMuonGNS
-    shapes = [tuple(int(x) for x in s.split("x")) for s in args.shape.split(",")]
-    peak_tf, _, peak_kind = peaks()
-    out = []
-    for (r, c) in shapes:
-        g = torch.Generator(device=dev).manual_seed(0)
-        U = torch.randn(14, r, c, generator=g, device=dev)
-        U = U / torch.linalg.matrix_norm(U, ord=2, keepdim=True)
-        U = U.to(torch.bfloat16)
-        opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=dev))], orthogonalizer=args.orthogonalizer,
-                         coefficients=args.coefficients)
-        o = torch.empty_like(U)
-        ws = opt._workspace(dev, 14, r, c)
-        part = ws["partial"].view(14, -1)
-        part.zero_()
-        part[:, 0] = U.float().pow(2).sum(dim=(1, 2))
-        for _ in range(args.warmup):
-            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
-        torch.cuda.synchronize()
-        s0 = torch.cuda.Event(enable_timing=True)
-        s1 = torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.steps):
-            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
-        s1.record()
-        torch.cuda.synchronize()
-        ms = s0.elapsed_time(s1) / args.steps
-        mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
-        fl = 14 * gram_flops(min(r, c), max(r, c), mode=mode)
-        tf = fl / (ms * 1e-3) / 1e12
-        out.append({"shape": f"14x{r}x{c}", "ms": ms, "tflops": tf, "frac": tf / peak_tf})
-    return {"metric": "Gram-NS TFLOP/s", "value": statistics.mean(x["tflops"] for x in out), "unit": "TFLOP/s",
-            "higher_is_better": True, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16/f16",
-            "data": "synthetic", "config": {"workload": "configs[2] Gram-NS microbenchmark",
-                                             "orthogonalizer": args.orthogonalizer, "coefficients": args.coefficients},
-            "per_shape": out, "peak": peak_tf, "peak_kind": f"{peak_kind} bf16 burst"}
-
-
-def micro_adamw(args, dev):
-    """streaming AdamW+EMA over 7 x 32768 x 1024 + 1M scalars,
-    bf16 params + bf16 remainder, fp32 moments, fp32 EMA, cautious decay 0.1, step 100."""
-    from sol_b200 import AdamW, EmaWeights
-    g = torch.Generator(device=dev).manual_seed(0)
-    params = [torch.nn.Parameter((torch.randn(32768, 1024, generator=g, device=dev) * 0.02).to(torch.bfloat16))
-              for _ in range(args.tables)]
-    params.append(torch.nn.Parameter(torch.ones(1 << 20, device=dev, dtype=torch.bfloat16)))
-    for p in params:
-        p.grad = (torch.randn(p.shape, generator=g, device=dev) * 1e-4).to(torch.bfloat16)
-    opt = AdamW(params, lr=2.4e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, master="bf16_mt",
-                cautious_wd=True)
-    holder = torch.nn.Module()
-    for i, p in enumerate(params):
-        holder.register_parameter(f"t{i}", p)
-    ema = EmaWeights(holder, 0.999)
-    for p in params:
-        opt._init_state(p)
-        opt._steps[id(p)] = 99
-    ema.update()  # arms folding
-    for _ in range(args.warmup):
-        opt.step()
-        ema.update()
-    torch.cuda.synchronize()
-    s0 = torch.cuda.Event(enable_timing=True)
-    s1 = torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(args.steps):
-        opt.step()
-        ema.update()
-    s1.record()
-    torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / args.steps
-    n = sum(p.numel() for p in params)
-    gbs = n * 34 / (ms * 1e-3) / 1e9
-    _, peak_gbs, peak_kind = peaks()
-    return {"metric": "AdamW+EMA GB/s", "value": gbs, "unit": "GB/s", "higher_is_better": True, "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "dtype": "bf16+fp32", "data": "synthetic",
-            "config": {"workload": "configs[3] streaming AdamW+EMA", "elements": n,
-                       "bytes_per_element": 34, "ema": "fp32 (bf16 shadow underflows at decay 0.999)"},
-            "ms_per_step": ms,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak_gbs, "unit": "GB/s", "frac": gbs / peak_gbs,
-                         "traffic": None, "peak_kind": f"{peak_kind} copy"}}
 
 
 def main():
@@ -512,6 +478,8 @@ def main():
     ap.add_argument("--config", default="c2_L14_d1024", choices=sorted(synth.CONFIGS))
     ap.add_argument("--orthogonalizer", default="gram", choices=["gram", "quintic"])
     ap.add_argument("--coefficients", default="polar_express", choices=["polar_express", "quintic"])
+    ap.add_argument("--exchange", default="auto", choices=["auto", "ce", "nccl"],
+                    help="N>1: copy-engine pushes over CUDA IPC mappings, or NCCL all-gathers")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gram", "adamw"], default=None,

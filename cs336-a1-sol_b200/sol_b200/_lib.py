@@ -107,6 +107,10 @@ SIGNATURES = {
     "b2o_gemm_bf16_simt": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
                                    c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
+    "b2o_ipc_export": (c_int, [c_void_p, c_void_p, C.POINTER(C.c_uint64)]),
+    "b2o_ipc_import": (c_int, [c_void_p, C.POINTER(c_void_p)]),
+    "b2o_ipc_close": (c_int, [c_void_p]),
+    "b2o_copy_async": (c_int, [C.POINTER(c_void_p), C.POINTER(c_void_p), C.POINTER(c_int64), c_int, c_void_p]),
 }
 
 _lib = None
@@ -185,3 +189,38 @@ def gemm_timing_read():
     ms, fl, n = C.c_double(), C.c_double(), c_int64()
     load().b2o_gemm_timing_read(C.byref(ms), C.byref(fl), C.byref(n))
     return ms.value, fl.value, n.value
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding ptr, ptr's offset in it)."""
+    lib = load()
+    buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+    off = C.c_uint64(0)
+    check(lib.b2o_ipc_export(ptr, buf, C.byref(off)), "ipc_export")
+    return buf.raw, off.value
+
+
+def ipc_import(handle: bytes) -> int:
+    """Maps another process's allocation into this one; returns its base pointer."""
+    lib = load()
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("IPC handle must be 64 bytes")
+    base = c_void_p(0)
+    check(lib.b2o_ipc_import(C.create_string_buffer(handle, IPC_HANDLE_BYTES), C.byref(base)), "ipc_import")
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    check(load().b2o_ipc_close(base), "ipc_close")
+
+
+def copy_async(copies, stream: int) -> None:
+    """Enqueues device-to-device copies [(dst_ptr, src_ptr, nbytes), ...] on stream."""
+    n = len(copies)
+    dst = ptr_array([d for d, _, _ in copies])
+    src = ptr_array([s for _, s, _ in copies])
+    nb = (c_int64 * max(1, n))(*[b for _, _, b in copies])
+    check(load().b2o_copy_async(dst, src, nb, n, stream), "copy_async")

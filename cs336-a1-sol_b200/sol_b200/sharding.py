@@ -13,11 +13,22 @@ so every rank's result is bit-identical to the single-GPU engine.
     scalar/gain tensors are updated redundantly by every rank (no exchange).
   * EMA: each rank folds the EMA of what it updates; shadows of other ranks'
     parameters are gathered on demand by gather_ema().
+
+Exchange inside step(): every rank pushes the rows it updated into the same
+offsets of every peer's copies with copy-engine transfers (CUDA IPC mappings,
+one stream per peer), the tables right after AdamW, so they cross NVLink while
+NorMuon computes, and the NorMuon arena at the end. Copy engines leave every SM
+to the GEMMs, where an all-gather kernel would take some and push the GEMMs'
+one-wave grids into a second wave. A one-element NCCL all-reduce after the
+pushes is the completion barrier. Where IPC export is not possible (memory from
+cuMemCreate, CPU tensors) step() uses NCCL all-gathers instead.
 """
 from __future__ import annotations
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 def gram_cost(shape) -> float:
@@ -39,7 +50,13 @@ def assign_matrices(shapes, world):
 
 
 class ShardedStep:
-    def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024):
+    def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024,
+                 exchange: str = "auto"):
+        """exchange: "auto" (copy-engine pushes where every rank can export
+        its buffers, else NCCL), "ce" (copy-engine pushes or an error) or
+        "nccl" (all-gathers)."""
+        if exchange not in ("auto", "ce", "nccl"):
+            raise ValueError("exchange must be 'auto', 'ce' or 'nccl'")
         self.world, self.rank, self.group = world, rank, group
         self.muon, self.adamw, self.ema = muon, adamw, ema
         mparams = [p for g in muon.param_groups for p in g["params"]]
@@ -53,6 +70,7 @@ class ShardedStep:
         align = 64
         sizes = [sum((p.numel() + align - 1) // align * align for p in ps) for ps in per_rank]
         self.chunk = max(sizes) if sizes else 0
+        self.arena_used = sizes  # elements of each rank's chunk that hold parameters
         self.arena = torch.empty(self.chunk * world, dtype=dt, device=dev)
         for r, ps in enumerate(per_rank):
             off = r * self.chunk
@@ -86,6 +104,99 @@ class ShardedStep:
                 if k is not None and k != rank:
                     skip.add(i)
             ema._skip = skip
+        self.exchange = "nccl"
+        self._bases = []
+        self._streams = []
+        self._plans = None
+        if world > 1 and exchange != "nccl":
+            self._setup_peer_exchange(required=exchange == "ce")
+
+    # ------------------------------------------------------------ layout ---
+    def buffers(self):
+        """Tensors exchanged between ranks: the NorMuon arena, then each row-sharded table."""
+        return [self.arena] + [p.data for p in self.row_sharded]
+
+    def owned_regions(self, rank: int):
+        """(buffer index, byte offset, bytes) of what `rank` updates in each exchanged buffer."""
+        es = self.arena.element_size()
+        regions = []
+        if self.chunk and self.arena_used[rank]:
+            regions.append((0, rank * self.chunk * es, self.arena_used[rank] * es))
+        for i, p in enumerate(self.row_sharded):
+            per = p.numel() // self.world
+            regions.append((1 + i, rank * per * p.element_size(), per * p.element_size()))
+        return regions
+
+    def _setup_peer_exchange(self, required: bool):
+        bufs = self.buffers()
+        dev = self.arena.device
+        mine = None
+        if dev.type == "cuda":
+            try:
+                with torch.cuda.device(dev):
+                    mine = [(*_lib.ipc_export(b.data_ptr()), b.numel() * b.element_size()) for b in bufs]
+            except RuntimeError:
+                mine = None
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=self.group)
+        if any(e is None for e in every):
+            if required:
+                raise RuntimeError("sharded step: copy-engine exchange needs CUDA IPC export on every rank")
+            return
+        for r, e in enumerate(every):
+            if [n for _, _, n in e] != [n for _, _, n in mine]:
+                raise RuntimeError(f"sharded step: rank {r} laid out its exchanged buffers differently")
+        opened = {}
+        peer_ptrs = {}
+        with torch.cuda.device(dev):
+            for q in range(self.world):
+                if q == self.rank:
+                    continue
+                ptrs = []
+                for handle, off, _ in every[q]:
+                    if handle not in opened:
+                        opened[handle] = _lib.ipc_import(handle)
+                        self._bases.append(opened[handle])
+                    ptrs.append(opened[handle] + off)
+                peer_ptrs[q] = ptrs
+            self._streams = {q: torch.cuda.Stream(dev) for q in peer_ptrs}
+        local = [b.data_ptr() for b in bufs]
+        tables, arena = {}, {}
+        for q, ptrs in peer_ptrs.items():
+            for k, off, nbytes in self.owned_regions(self.rank):
+                (arena if k == 0 else tables).setdefault(q, []).append((ptrs[k] + off, local[k] + off, nbytes))
+        self._plans = {"tables": tables, "arena": arena}
+        self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.exchange = "ce"
+
+    def _push(self, which):
+        cur = torch.cuda.current_stream()
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        for q, copies in self._plans[which].items():
+            st = self._streams[q]
+            st.wait_event(ev)
+            _lib.copy_async(copies, st.cuda_stream)
+
+    def _finish_pushes(self):
+        cur = torch.cuda.current_stream()
+        for st in self._streams.values():
+            cur.wait_stream(st)
+        # every rank reaches this collective only after its own pushes landed
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self):
+        """Unmaps the peers' buffers (call on every rank before freeing the model)."""
+        if not self._bases:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for b in self._bases:
+            _lib.ipc_close(b)
+        self._bases = []
+        self._plans = None
+        self.exchange = "nccl"
+        dist.barrier(group=self.group)
 
     def _gather_tables(self, async_op=False):
         works = []
@@ -113,20 +224,35 @@ class ShardedStep:
         self._gather_tables()
 
     @torch.no_grad()
-    def step(self):
+    def step(self, mark=None):
         """One sharded optimizer step: AdamW first, so the all-gathers of the
         vocabulary tables run on NCCL's stream while NorMuon computes; then
         NorMuon, the EMA update and the all-gather of the NorMuon arena.
-        Same results as muon.step(); adamw.step(); ema.update(); gather()."""
+        Same results as muon.step(); adamw.step(); ema.update(); gather().
+        ``mark(name)``, when given, is called after each phase is enqueued
+        (phase timing with events on the current stream)."""
+        mark = mark or (lambda name: None)
+        ce = self.exchange == "ce"
         self.adamw.step()
-        works = self._gather_tables(async_op=True) if self.world > 1 else []
+        mark("adamw")
+        works = []
+        if ce:
+            self._push("tables")
+        elif self.world > 1:
+            works = self._gather_tables(async_op=True)
         self.muon.step()
+        mark("normuon")
         if self.ema is not None:
             self.ema.update()
-        if self.world > 1:
+        if ce:
+            self._push("arena")
+            self._finish_pushes()
+        elif self.world > 1:
             self._gather_arena()
+        mark("arena_gather")
         for w in works:
             w.wait()
+        mark("table_wait")
 
     @torch.no_grad()
     def gather_ema(self):

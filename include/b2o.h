@@ -237,6 +237,30 @@ int b2o_gemm_bf16_simt(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_
                        float alpha, float beta, float gamma, const float* d_scale,
                        float* d_rowsq, void* stream);
 
+/* ------------------------------------------------------------------------ *
+ * Peer exchange for the sharded step on the GPUs of one node (no reference
+ * counterpart: the reference is single-GPU, transformer_lm/train_sol.py has no
+ * torch.distributed call). Each rank pushes the parameter rows it updated into
+ * the same offsets of every other rank's copy with copy-engine transfers over
+ * NVLink, replacing an all-gather kernel that would occupy SMs next to the
+ * NorMuon GEMMs. The exchange of handles between processes and the completion
+ * barrier stay with the host's process group.
+ *
+ * b2o_ipc_export: writes the 64-byte CUDA IPC handle of the allocation holding
+ *   d_ptr and d_ptr's byte offset inside it (memory from cudaMalloc, which is
+ *   what PyTorch's caching allocator uses by default).
+ * b2o_ipc_import: maps another process's allocation into this process (current
+ *   device, peer access enabled on first use) and returns its base; open each
+ *   handle once per process and close it with b2o_ipc_close before the owner
+ *   frees the memory.
+ * b2o_copy_async: enqueues n device-to-device copies d_dst[i] <- d_src[i] of
+ *   bytes[i] bytes on `stream`, one cudaMemcpyAsync each, in order. */
+#define B2O_IPC_HANDLE_BYTES 64
+int b2o_ipc_export(const void* d_ptr, void* handle_out, uint64_t* offset_out);
+int b2o_ipc_import(const void* handle, void** d_base_out);
+int b2o_ipc_close(void* d_base);
+int b2o_copy_async(void* const* d_dst, const void* const* d_src, const int64_t* bytes, int n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
