@@ -275,7 +275,7 @@ def engine_arm(args, world, rank, local):
                                    adam_master="bf16_mt", **RECIPE)
     ema = EmaWeights(model, 0.999)
     sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank,
-                          exchange=args.exchange) if world > 1 else None
+                          exchange=args.exchange, push_streams=args.push_streams) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     ortho_events = []
     adam_ev = []
@@ -385,7 +385,8 @@ def engine_arm(args, world, rank, local):
                    "adamw": "bf16 + bf16 remainder, fp32 moments", "ema": "fp32, folded",
                    "l2": "working set > L2 (126 MB); no flush",
                    "parallelism": f"shard{world}" if world > 1 else "single",
-                   "exchange": sharded.exchange if sharded is not None else None},
+                   "exchange": sharded.exchange if sharded is not None else None,
+                   "push_streams": sharded.push_streams if sharded is not None else None},
         "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
                       "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
         "sharded_phases_ms": shard_phases or None,
@@ -478,8 +479,9 @@ def main():
     ap.add_argument("--config", default="c2_L14_d1024", choices=sorted(synth.CONFIGS))
     ap.add_argument("--orthogonalizer", default="gram", choices=["gram", "quintic"])
     ap.add_argument("--coefficients", default="polar_express", choices=["polar_express", "quintic"])
-    ap.add_argument("--exchange", default="auto", choices=["auto", "ce", "nccl"],
-                    help="N>1: copy-engine pushes over CUDA IPC mappings, or NCCL all-gathers")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "ce", "hybrid", "nccl"],
+                    help="N>1: copy-engine pushes over CUDA IPC mappings, NCCL all-gathers, or both")
+    ap.add_argument("--push-streams", type=int, default=1, help="N>1: streams the copy-engine pushes use")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--micro", choices=["gram", "adamw"], default=None,

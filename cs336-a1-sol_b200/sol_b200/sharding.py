@@ -15,13 +15,17 @@ so every rank's result is bit-identical to the single-GPU engine.
     parameters are gathered on demand by gather_ema().
 
 Exchange inside step(): every rank pushes the rows it updated into the same
-offsets of every peer's copies with copy-engine transfers (CUDA IPC mappings,
-one stream per peer), the tables right after AdamW, so they cross NVLink while
-NorMuon computes, and the NorMuon arena at the end. Copy engines leave every SM
-to the GEMMs, where an all-gather kernel would take some and push the GEMMs'
-one-wave grids into a second wave. A one-element NCCL all-reduce after the
-pushes is the completion barrier. Where IPC export is not possible (memory from
-cuMemCreate, CPU tensors) step() uses NCCL all-gathers instead.
+offsets of every peer's copies with copy-engine transfers (CUDA IPC mappings),
+visiting the peers in ring order so that each rank sends to one peer at a time
+(all peers at once left the copy engines at ~300 GB/s on 8 GPUs). The tables
+are pushed right after AdamW, so they cross NVLink while NorMuon computes: copy
+engines leave every SM to the GEMMs, where an all-gather kernel would take
+some and push the GEMMs' one-wave grids into a second wave. The NorMuon arena,
+ready only at the end, goes by copy-engine push on two ranks ("ce", then a
+one-element NCCL all-reduce as the completion barrier) and by NCCL all-gather
+from four ranks on ("hybrid"; the all-gather is then also the pushes'
+barrier). Where IPC export is not possible (memory from cuMemCreate, CPU
+tensors) step() uses NCCL all-gathers only.
 """
 from __future__ import annotations
 
@@ -51,13 +55,25 @@ def assign_matrices(shapes, world):
 
 class ShardedStep:
     def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024,
-                 exchange: str = "auto"):
-        """exchange: "auto" (copy-engine pushes where every rank can export
-        its buffers, else NCCL), "ce" (copy-engine pushes or an error) or
-        "nccl" (all-gathers)."""
-        if exchange not in ("auto", "ce", "nccl"):
-            raise ValueError("exchange must be 'auto', 'ce' or 'nccl'")
+                 exchange: str = "auto", push_streams: int = 1):
+        """exchange: "ce" (copy-engine pushes of the tables and the arena),
+        "hybrid" (copy-engine pushes of the tables, overlapped with NorMuon;
+        NCCL all-gather of the arena), "nccl" (all-gathers only) or "auto".
+        Copy-engine modes fall back to NCCL where a rank cannot export its
+        buffers ("auto") or raise. push_streams: streams the pushes are spread
+        over; peers are visited in ring order rank+1, rank+2, ... so with one
+        stream every rank sends to one peer at a time."""
+        if exchange not in ("auto", "ce", "hybrid", "nccl"):
+            raise ValueError("exchange must be 'auto', 'ce', 'hybrid' or 'nccl'")
+        required = exchange != "auto"
+        if exchange == "auto":
+            # measured on 8xB200 (C2 step): with one peer the arena push beats
+            # NCCL's all-gather; from four ranks on NCCL's all-gather of the
+            # arena is faster than copy-engine pushes, and the table pushes stay
+            # on the copy engines (overlapped with NorMuon, no SMs taken)
+            exchange = "ce" if world <= 2 else "hybrid"
         self.world, self.rank, self.group = world, rank, group
+        self.push_streams = max(1, min(int(push_streams), max(1, world - 1)))
         self.muon, self.adamw, self.ema = muon, adamw, ema
         mparams = [p for g in muon.param_groups for p in g["params"]]
         owner, self.load = assign_matrices([tuple(p.shape) for p in mparams], world)
@@ -108,8 +124,9 @@ class ShardedStep:
         self._bases = []
         self._streams = []
         self._plans = None
+        self._requested = exchange
         if world > 1 and exchange != "nccl":
-            self._setup_peer_exchange(required=exchange == "ce")
+            self._setup_peer_exchange(required=required)
 
     # ------------------------------------------------------------ layout ---
     def buffers(self):
@@ -142,7 +159,7 @@ class ShardedStep:
         if any(e is None for e in every):
             if required:
                 raise RuntimeError("sharded step: copy-engine exchange needs CUDA IPC export on every rank")
-            return
+            return  # NCCL all-gathers on every rank (all ranks saw the same list)
         for r, e in enumerate(every):
             if [n for _, _, n in e] != [n for _, _, n in mine]:
                 raise RuntimeError(f"sharded step: rank {r} laid out its exchanged buffers differently")
@@ -159,31 +176,32 @@ class ShardedStep:
                         self._bases.append(opened[handle])
                     ptrs.append(opened[handle] + off)
                 peer_ptrs[q] = ptrs
-            self._streams = {q: torch.cuda.Stream(dev) for q in peer_ptrs}
+            self._streams = [torch.cuda.Stream(dev) for _ in range(self.push_streams)]
         local = [b.data_ptr() for b in bufs]
-        tables, arena = {}, {}
-        for q, ptrs in peer_ptrs.items():
+        # per stream, the copies in ring order of the peers
+        plans = {"tables": [[] for _ in self._streams], "arena": [[] for _ in self._streams]}
+        for d in range(1, self.world):
+            q = (self.rank + d) % self.world
             for k, off, nbytes in self.owned_regions(self.rank):
-                (arena if k == 0 else tables).setdefault(q, []).append((ptrs[k] + off, local[k] + off, nbytes))
-        self._plans = {"tables": tables, "arena": arena}
+                which = "arena" if k == 0 else "tables"
+                plans[which][(d - 1) % self.push_streams].append((peer_ptrs[q][k] + off, local[k] + off, nbytes))
+        self._plans = plans
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
-        self.exchange = "ce"
+        self.exchange = self._requested
 
     def _push(self, which):
         cur = torch.cuda.current_stream()
         ev = torch.cuda.Event()
         ev.record(cur)
-        for q, copies in self._plans[which].items():
-            st = self._streams[q]
-            st.wait_event(ev)
-            _lib.copy_async(copies, st.cuda_stream)
+        for st, copies in zip(self._streams, self._plans[which]):
+            if copies:
+                st.wait_event(ev)
+                _lib.copy_async(copies, st.cuda_stream)
 
-    def _finish_pushes(self):
+    def _join_pushes(self):
         cur = torch.cuda.current_stream()
-        for st in self._streams.values():
+        for st in self._streams:
             cur.wait_stream(st)
-        # every rank reaches this collective only after its own pushes landed
-        dist.all_reduce(self._flag, group=self.group)
 
     def close(self):
         """Unmaps the peers' buffers (call on every rank before freeing the model)."""
@@ -232,11 +250,11 @@ class ShardedStep:
         ``mark(name)``, when given, is called after each phase is enqueued
         (phase timing with events on the current stream)."""
         mark = mark or (lambda name: None)
-        ce = self.exchange == "ce"
+        push_tables = self.exchange in ("ce", "hybrid")
         self.adamw.step()
         mark("adamw")
         works = []
-        if ce:
+        if push_tables:
             self._push("tables")
         elif self.world > 1:
             works = self._gather_tables(async_op=True)
@@ -244,10 +262,15 @@ class ShardedStep:
         mark("normuon")
         if self.ema is not None:
             self.ema.update()
-        if ce:
+        if self.exchange == "ce":
             self._push("arena")
-            self._finish_pushes()
+            self._join_pushes()
+            # every rank enters this collective only after its own pushes
+            # landed, so its completion means every rank's pushes did
+            dist.all_reduce(self._flag, group=self.group)
         elif self.world > 1:
+            if push_tables:
+                self._join_pushes()  # the arena all-gather is then also the pushes' barrier
             self._gather_arena()
         mark("arena_gather")
         for w in works:

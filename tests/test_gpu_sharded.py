@@ -77,7 +77,7 @@ def _worker(rank, world, port, exchange, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["ce", "nccl"])
+@pytest.mark.parametrize("exchange", ["ce", "hybrid", "nccl"])
 def test_sharded_step_bit_identical_to_single_gpu(exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
