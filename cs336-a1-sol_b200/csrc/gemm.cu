@@ -536,10 +536,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN;
       uint32_t cur[32], nxt[32];
+      // C rows (KIND != 0) are fetched one chunk ahead, like the accumulator,
+      // so their L2 latency overlaps the current chunk's arithmetic and stores
+      uint4 craw[4], cnext[4];
+      auto c_fetch = [&](int chn, uint4* dst) {
+        const int cc0 = tn * BN + chn * 32;
+        if (KIND != 0 && row < p.M && vec_c && cc0 + 32 <= p.N) {
+          const uint4* src = reinterpret_cast<const uint4*>(Cb + static_cast<int64_t>(row) * e.ldc + cc0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) dst[q] = src[q];
+        }
+      };
       int ch = todo ? __ffs(todo) - 1 : -1;
       if (ch >= 0) {
         __syncwarp();
         tmem_ld32_issue(tbase + ch * 32, cur);
+        c_fetch(ch, craw);
         tmem_ld_wait();
       }
       int slot = 0;
@@ -547,15 +559,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       while (ch >= 0) {
         const uint32_t rest = todo & ~((2u << ch) - 1u);
         const int nch = rest ? __ffs(rest) - 1 : -1;
-        if (nch >= 0) tmem_ld32_issue(tbase + nch * 32, nxt);  // overlaps this chunk's work
+        if (nch >= 0) {
+          tmem_ld32_issue(tbase + nch * 32, nxt);  // overlaps this chunk's work
+          c_fetch(nch, cnext);
+        }
         const int c0 = tn * BN + ch * 32;
         const bool diag = SYM && (c0 == r0);
         float cv[32];
         if (KIND != 0) {
-          if (row < p.M) load_row32(Cb, e.ldc, row, c0, p.M, p.N, vec_c && (c0 + 32 <= p.N), DHALF, cv);
-          else {
+          if (row >= p.M) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) cv[j] = 0.f;
+          } else if (vec_c && (c0 + 32 <= p.N)) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t w[4] = {craw[q].x, craw[q].y, craw[q].z, craw[q].w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                cv[q * 8 + 2 * h] = h16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu), DHALF);
+                cv[q * 8 + 2 * h + 1] = h16_to_f32(static_cast<uint16_t>(w[h] >> 16), DHALF);
+              }
+            }
+          } else {
+            load_row32(Cb, e.ldc, row, c0, p.M, p.N, false, DHALF, cv);
           }
         }
         uint32_t pk[16];
@@ -609,6 +635,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; ++j) cur[j] = nxt[j];
+          if (KIND != 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) craw[q] = cnext[q];
+          }
         }
         ch = nch;
       }

@@ -24,6 +24,9 @@
 #include "b2o_internal.h"
 
 #include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
 #include <vector>
 
 namespace b2o {
@@ -136,6 +139,198 @@ __global__ void ns_normalize_kernel(const uint16_t* __restrict__ U, uint16_t* __
     x[i] = f32_to_bf16(__fdiv_rn(bf16_to_f32(u[i]), d));
 }
 
+// ---------------------------------------------------------------------------
+// Small matrices (m = min(r, c) <= 32, m * n <= kSmallElems): the whole Gram
+// Newton-Schulz iteration of one matrix runs in one CTA out of shared memory
+// (the recipe's 8 x 1024 attention gates would otherwise take ~20 launches of
+// tiny GEMMs). Same schedule and the same binary16 rounding points as the
+// tensor-core path: X0 = f16(u * s); R = sym f16(X X^T); P = sym f16(c R^2 +
+// b R + a I); Q = f16(Q P); R <- sym f16(f16(P R) P); X1 = f16(Q X0) and
+// R = sym f16(X1 X1^T) at restarts; o = bf16(Q X) with row sums of o^2 per
+// 256-column tile. Symmetric results take the upper triangle, as the
+// tensor-core epilogue's mirror does. Accumulation is fp32.
+constexpr int kSmallM = 32;
+constexpr int kSmallElems = 49152;  // two binary16 m x n iterates in <= 192 KB of shared memory
+constexpr int kSmallThreads = 256;
+
+struct SmallNsArgs {
+  float coef[3 * 64];
+  unsigned long long resets;  // bit t: restart at step t
+  int T;
+  int r, c, m, n, tall, nparts, ntn;
+  float eps, safety;
+};
+
+// C = A B^T or A B for m x m row-major float matrices in shared memory, each
+// result rounded to binary16; sym: compute i <= j and mirror.
+__device__ void small_mm(const float* A, const float* B, float* C, int m, bool b_transposed, bool sym) {
+  const int total = m * m;
+  for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+    const int i = idx / m, j = idx - (idx / m) * m;
+    if (sym && i > j) continue;
+    float acc = 0.f;
+    for (int k = 0; k < m; ++k) acc = fmaf(A[i * m + k], b_transposed ? B[j * m + k] : B[k * m + j], acc);
+    const float v = f16_to_f32(f32_to_f16(acc));
+    C[i * m + j] = v;
+    if (sym) C[j * m + i] = v;
+  }
+}
+
+// R = sym f16(X X^T) for X (m x n, binary16 in shared memory), one warp per entry
+__device__ void small_gram(const uint16_t* X, float* R, int m, int n) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int pairs = m * (m + 1) / 2;
+  for (int pidx = warp; pidx < pairs; pidx += nw) {
+    int i = 0, rem = pidx;
+    while (rem >= m - i) { rem -= m - i; ++i; }
+    const int j = i + rem;
+    float acc = 0.f;
+    for (int k = lane; k < n; k += 32) acc = fmaf(f16_to_f32(X[i * n + k]), f16_to_f32(X[j * n + k]), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const float v = f16_to_f32(f32_to_f16(acc));
+      R[i * m + j] = v;
+      R[j * m + i] = v;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSmallThreads) small_gram_ns_kernel(
+    const uint16_t* __restrict__ U, const float* __restrict__ partial, uint16_t* __restrict__ out,
+    float* __restrict__ rowsq, const __grid_constant__ SmallNsArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int m = a.m, n = a.n, mm = m * m;
+  uint16_t* X0 = reinterpret_cast<uint16_t*>(sm);
+  uint16_t* X1 = X0 + m * n;
+  float* R = reinterpret_cast<float*>(X1 + m * n);
+  float* P = R + mm;
+  float* Q = P + mm;
+  float* Tm = Q + mm;
+  float* Rn = Tm + mm;
+  float* red = Rn + mm;  // 32 floats
+  const int s = blockIdx.x;
+  const int64_t rc = static_cast<int64_t>(a.r) * a.c;
+  pdl_wait();
+  // scale s = 1 / (||u|| * safety + eps) from the front's partial sums of u^2
+  if (threadIdx.x == 0) {  // summed in the order norm_finalize_kernel uses
+    float acc = 0.f;
+    for (int i = 0; i < a.nparts; ++i) acc += partial[static_cast<int64_t>(s) * a.nparts + i];
+    red[0] = 1.0f / (sqrtf(acc) * a.safety + a.eps);
+  }
+  __syncthreads();
+  const float sc = red[0];
+  // X0[i][k] = f16(u * s), i on the m side (rows of u when wide, columns when tall)
+  const uint16_t* u = U + static_cast<int64_t>(s) * rc;
+  for (int idx = threadIdx.x; idx < m * n; idx += blockDim.x) {
+    const int i = idx / n, k = idx - (idx / n) * n;
+    const uint16_t v = a.tall ? u[static_cast<int64_t>(k) * a.c + i] : u[static_cast<int64_t>(i) * a.c + k];
+    X0[idx] = f32_to_f16(bf16_to_f32(v) * sc);
+  }
+  __syncthreads();
+  small_gram(X0, R, m, n);
+  __syncthreads();
+  const uint16_t* X = X0;
+  bool have_q = false;
+  for (int t = 0; t < a.T; ++t) {
+    const float ca = a.coef[3 * t], cb = a.coef[3 * t + 1], cc = a.coef[3 * t + 2];
+    if (t > 0 && ((a.resets >> t) & 1ull)) {
+      // X1 = f16(Q X), R = sym f16(X1 X1^T)
+      for (int idx = threadIdx.x; idx < m * n; idx += blockDim.x) {
+        const int i = idx / n, k = idx - (idx / n) * n;
+        float acc = 0.f;
+        for (int j = 0; j < m; ++j) acc = fmaf(Q[i * m + j], f16_to_f32(X[j * n + k]), acc);
+        X1[idx] = f32_to_f16(acc);
+      }
+      __syncthreads();
+      X = X1;
+      small_gram(X, R, m, n);
+      __syncthreads();
+      have_q = false;
+    }
+    // P = sym f16(c R^2 + b R + a I)
+    for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) {
+      const int i = idx / m, j = idx - (idx / m) * m;
+      if (i > j) continue;
+      float acc = 0.f;
+      for (int k = 0; k < m; ++k) acc = fmaf(R[i * m + k], R[j * m + k], acc);
+      const float v = f16_to_f32(f32_to_f16(fmaf(cc, acc, fmaf(cb, R[i * m + j], i == j ? ca : 0.f))));
+      P[i * m + j] = v;
+      P[j * m + i] = v;
+    }
+    __syncthreads();
+    if (!have_q) {
+      for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) Q[idx] = P[idx];
+      have_q = true;
+    } else {
+      small_mm(Q, P, Tm, m, false, false);  // Tm = f16(Q P)
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) Q[idx] = Tm[idx];
+    }
+    __syncthreads();
+    const bool need_r = (t < a.T - 1) && !((a.resets >> (t + 1)) & 1ull);
+    if (need_r) {
+      small_mm(P, R, Tm, m, false, false);  // f16(P R)
+      __syncthreads();
+      small_mm(Tm, P, Rn, m, false, true);  // sym f16((P R) P)
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) R[idx] = Rn[idx];
+      __syncthreads();
+    }
+  }
+  // o = bf16(Q X) in the stored (r, c) layout (also kept in the free iterate
+  // buffer), then the row sums of o^2 per 256-column tile in column order
+  uint16_t* o = out + static_cast<int64_t>(s) * rc;
+  uint16_t* Ob = (X == X0) ? X1 : X0;
+  for (int idx = threadIdx.x; idx < m * n; idx += blockDim.x) {
+    // wide: idx walks stored rows i, columns k; tall: stored rows k, columns i
+    const int i = a.tall ? idx % m : idx / n;
+    const int k = a.tall ? idx / m : idx % n;
+    float acc = 0.f;
+    for (int j = 0; j < m; ++j) acc = fmaf(Q[i * m + j], f16_to_f32(X[j * n + k]), acc);
+    const uint16_t ob = f32_to_bf16(acc);
+    Ob[i * n + k] = ob;
+    o[a.tall ? static_cast<int64_t>(k) * a.c + i : static_cast<int64_t>(i) * a.c + k] = ob;
+  }
+  __syncthreads();
+  if (!a.tall) {
+    for (int w = threadIdx.x; w < m * a.ntn; w += blockDim.x) {
+      const int i = w / a.ntn, tn = w - (w / a.ntn) * a.ntn;
+      float part = 0.f;
+      for (int k = tn * 256; k < min(n, tn * 256 + 256); ++k) {
+        const float y = bf16_to_f32(Ob[i * n + k]);
+        part = fmaf(y, y, part);
+      }
+      rowsq[(static_cast<int64_t>(s) * a.ntn + tn) * a.r + i] = part;
+    }
+  } else {
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+      float part = 0.f;
+      for (int i = 0; i < m; ++i) {
+        const float y = bf16_to_f32(Ob[i * n + k]);
+        part = fmaf(y, y, part);
+      }
+      rowsq[static_cast<int64_t>(s) * a.r + k] = part;
+    }
+  }
+}
+
+// Opts the small-matrix kernel into more than 48 KB of dynamic shared memory
+// (once per device).
+static int small_ns_smem_optin(int bytes) {
+  static std::mutex mu;
+  static int done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { set_error("small_gram_ns: no device"); return -1; }
+  std::lock_guard<std::mutex> lk(mu);
+  if (bytes <= 48 * 1024 || done[dev]) return 0;
+  cudaError_t e = cudaFuncSetAttribute(small_gram_ns_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (2 * kSmallElems * 2 + 5 * kSmallM * kSmallM * 4 + 32 * 4));
+  if (e != cudaSuccess) { set_error(std::string("small_gram_ns: ") + cudaGetErrorString(e)); return static_cast<int>(e); }
+  done[dev] = 1;
+  return 0;
+}
+
 namespace {
 
 struct Batch {
@@ -223,6 +418,30 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   auto xb = [&](int g) { return reinterpret_cast<uint16_t*>(base + L.xb_off[g]); };
   float* scal = reinterpret_cast<float*>(base + L.scal_off);
 
+  // small matrices: one kernel per group does the whole iteration
+  bool small = mode == 1 && L.m <= kSmallM;
+  for (int g = 0; g < ng; ++g) small = small && static_cast<int64_t>(bg[g].m) * bg[g].n <= kSmallElems;
+  if (small) {
+    SmallNsArgs sa;
+    memset(&sa, 0, sizeof(sa));
+    for (int i = 0; i < 3 * T; ++i) sa.coef[i] = coeffs[i];
+    for (int i = 0; i < nresets; ++i)
+      if (resets[i] > 0 && resets[i] < 64) sa.resets |= 1ull << resets[i];
+    sa.T = T; sa.eps = norm_eps; sa.safety = norm_safety;
+    for (int g = 0; g < ng; ++g) {
+      const Batch& b = bg[g];
+      sa.r = b.r; sa.c = b.c; sa.m = b.m; sa.n = b.n; sa.tall = b.tall ? 1 : 0;
+      sa.nparts = normuon_front_parts(b.rc);
+      sa.ntn = (b.c + 255) / 256;
+      const int smem = static_cast<int>(2 * b.m * b.n * 2 + 5 * b.mm * 4 + 32 * 4);
+      if (int e = small_ns_smem_optin(smem)) return e;
+      launch_pdl(small_gram_ns_kernel, dim3(b.S), dim3(kSmallThreads), static_cast<size_t>(smem), stream,
+                 groups[g].U, groups[g].partial, groups[g].out, groups[g].rowsq, sa);
+      count_launch();
+      if (int e = check_launch("small_gram_ns")) return e;
+    }
+    return 0;
+  }
   for (int g = 0; g < ng; ++g) {
     const int nparts = normuon_front_parts(bg[g].rc);
     launch_pdl(norm_finalize_kernel, dim3((bg[g].S + 127) / 128), dim3(128), 0, stream, groups[g].partial, nparts,

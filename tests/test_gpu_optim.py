@@ -329,3 +329,25 @@ def test_ema_folded_equals_standalone(cuda):
             assert torch.equal(p.data, s.to(p.dtype))
     for p, b in zip(m1.parameters(), before):
         assert torch.equal(p.data, b)
+
+
+@pytest.mark.parametrize("r,c", [(8, 1024), (1024, 8), (32, 1536), (12, 4096), (33, 1024)])
+def test_gram_small_matrices_match_binary16_emulation(cuda, r, c):
+    """Matrices with min(r, c) <= 32 and at most 49152 elements run the whole
+    iteration in one CTA per matrix (the recipe's 8 x 1024 attention gates);
+    (33, 1024) takes the GEMM path. Both follow the CPU binary16 emulation of
+    the same schedule up to fp32 accumulation order."""
+    g = torch.Generator().manual_seed(7 * r + c)
+    U = (torch.randn(5, r, c, generator=g) * 1e-3).to(torch.bfloat16)
+    opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=cuda))], orthogonalizer="gram",
+                     coefficients="polar_express")
+    out = opt._orthogonalize_batch(U.cuda(), 5)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    table = polar_express.polar_express(5)
+    emu16 = gram_ns_ref.gram_ns(U, table, safety=opt.norm_safety, store=torch.float16)
+    ref64 = gram_ns_ref.gram_ns(U, table, safety=opt.norm_safety)
+    err, err64 = rel_fro(out.float(), emu16), rel_fro(out.float(), ref64)
+    print(f"({r},{c}) engine vs binary16 emulation {err:.2e}, vs fp64 {err64:.2e}")
+    assert err < 1e-2
+    assert err64 < 3e-2
