@@ -130,10 +130,10 @@ def gram_flops(m, n, T=5, resets=(2,), mode="gram"):
             q_is_identity = True
         f += m ** 3  # R^2 (symmetric)
         if not q_is_identity:
-            f += 2 * m ** 3
+            f += m ** 3  # Q P (symmetric: Q and P are polynomials in one Gram matrix)
         q_is_identity = False
         if t < T - 1 and (t + 1) not in resets:
-            f += 3 * m ** 3  # P R (full) and (P R) P (symmetric)
+            f += 2 * m ** 3  # P R and (P R) P (both symmetric)
     return f + 2 * m * m * n  # out = Q X
 
 

@@ -10,7 +10,8 @@
 //     symmetric outputs compute only tiles that touch the upper triangle and
 //     mirror them in the epilogue;
 //   * warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (and TMEM owner),
-//     warps 2-5 = epilogue (one TMEM lane quadrant each).
+//     warps 2-9 = epilogue (two per TMEM lane quadrant, half the columns each;
+//     warps 2-5 only, whole rows, for outputs with row sums).
 // Every wait is bounded: on expiry the CTA raises the device error word,
 // drains its own copies and MMAs (again bounded), frees TMEM and returns.
 // A CUDA-core kernel covers shapes the tensor-core path does not take
@@ -31,29 +32,34 @@ namespace tc {
 
 constexpr int BM = 128, BN = 256, BK = 64;     // BM: rows of one CTA's accumulator
 constexpr int A_BYTES = BM * BK * 2;            // 16 KB
-// PAIR = 1: one CTA computes a 128 x 256 tile (4 stages of 16 + 32 KB).
-// PAIR = 2: a CTA pair (cluster of 2, tcgen05 cta_group::2) computes a
-// 256 x 256 tile; each CTA stages its 128 rows of A and its 128 columns of B
-// (6 stages of 16 + 16 KB), halving the operand bytes each SM pulls per MMA.
-template <int PAIR> struct Geo {
-  static constexpr int B_ROWS = BN / PAIR;
-  static constexpr int B_BYTES = B_ROWS * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR == 1 ? 4 : 6;
-  static constexpr int TILE_M = BM * PAIR;
-};
-constexpr int STAGE_AREA = 4 * (A_BYTES + BN * BK * 2);  // 192 KB for either geometry
-static_assert(Geo<1>::STAGES * Geo<1>::STAGE_BYTES == STAGE_AREA, "stage area");
-static_assert(Geo<2>::STAGES * Geo<2>::STAGE_BYTES == STAGE_AREA, "stage area");
-constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;                  // 2 accumulators x 256 fp32 columns
 // Epilogue staging: per epilogue warp two slots of two 32x32 16-bit tiles
 // (direct and mirrored), 64-byte rows in the TMA 64-byte swizzle, written by
 // TMA stores; while one slot's stores drain the next chunk fills the other.
 constexpr int EPI_TILE_BYTES = 32 * 32 * 2;
 constexpr int EPI_WARP_BYTES = 2 * 2 * EPI_TILE_BYTES;  // 8 KB
-constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;           // 32 KB
-constexpr int SMEM_BYTES = STAGE_AREA + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// Epilogue warps: two per TMEM lane quadrant (each moves half of the 256
+// accumulator columns), except for outputs with row sums, whose partials are
+// per 256-column tile and row, kept whole by one warp per quadrant.
+template <int RSQ> struct EpiWarps { static constexpr int value = RSQ ? 4 : 8; };
+// PAIR = 1: one CTA computes a 128 x 256 tile (stages of 16 + 32 KB).
+// PAIR = 2: a CTA pair (cluster of 2, tcgen05 cta_group::2) computes a
+// 256 x 256 tile; each CTA stages its 128 rows of A and its 128 columns of B
+// (stages of 16 + 16 KB), halving the operand bytes each SM pulls per MMA.
+// The operand ring takes what shared memory leaves beside the epilogue staging.
+template <int PAIR, int EW> struct Geo {
+  static constexpr int B_ROWS = BN / PAIR;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_BYTES = EW * EPI_WARP_BYTES;
+  static constexpr int STAGES = PAIR == 1 ? (EW == 8 ? 3 : 4) : (EW == 8 ? 5 : 6);
+  static constexpr int STAGE_AREA = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGE_AREA + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int TILE_M = BM * PAIR;
+  static constexpr int THREADS = 64 + 32 * EW;  // TMA warp, MMA warp, epilogue warps
+};
+static_assert(Geo<1, 4>::SMEM_BYTES <= 232448 && Geo<1, 8>::SMEM_BYTES <= 232448, "shared memory");
+static_assert(Geo<2, 4>::SMEM_BYTES <= 232448 && Geo<2, 8>::SMEM_BYTES <= 232448, "shared memory");
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
 struct Params {
@@ -323,16 +329,17 @@ __device__ __forceinline__ float unpack_hi(uint32_t w) {
 }
 
 template <int KIND, int DHALF, int SYM, int RSQ, int PAIR>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__((Geo<PAIR, EpiWarps<RSQ>::value>::THREADS), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ Params p) {
-  using G = Geo<PAIR>;
+  constexpr int EW = EpiWarps<RSQ>::value;
+  using G = Geo<PAIR, EW>;
   constexpr int STAGES = G::STAGES;
   constexpr int STAGE_BYTES = G::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_smem = smem + STAGE_AREA;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + EPI_BYTES);
+  uint8_t* epi_smem = smem + G::STAGE_AREA;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + G::EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -350,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // full: one expect-tx arrival per CTA of the pair (counted on the MMA CTA);
     // tempty: every epilogue thread of the pair releases the accumulator
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full_bar[s], PAIR); mbar_init(&empty_bar[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 128 * PAIR); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 32 * EW * PAIR); }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -499,12 +506,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // --------------------------------------------------------- epilogue ---
     // Each warp owns TMEM lanes [32*quad, 32*quad+32), i.e. 32 output rows, and
-    // moves them out 32 columns at a time: tcgen05.ld -> epilogue arithmetic in
+    // a contiguous range of the 256 columns (all of them with 4 epilogue warps,
+    // one half with 8), moved out 32 columns at a time: tcgen05.ld -> epilogue arithmetic in
     // registers -> swizzled staging tile in shared memory -> TMA store (which
     // clips rows/columns outside the matrix). Symmetric outputs skip chunks
     // below the diagonal, store chunks above it twice (direct and mirrored)
     // and symmetrise the diagonal chunk in shared memory before one store.
     const int quad = warp & 3;
+    constexpr int CPW = (BN / 32) / (EW / 4);     // chunks of 32 columns per warp
+    const int ch_lo = ((warp - 2) >> 2) * CPW;    // this warp's first chunk
     const uint32_t st_base = smem_u32(epi_smem) + static_cast<uint32_t>(warp - 2) * EPI_WARP_BYTES;
     const uint32_t tempty0 = PAIR == 2 ? map_to_rank(smem_u32(&tempty_bar[0]), 0) : 0u;
     const uint32_t tempty1 = PAIR == 2 ? map_to_rank(smem_u32(&tempty_bar[1]), 0) : 0u;
@@ -529,7 +539,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // symmetric outputs, on or above the diagonal
       uint32_t todo = 0;
 #pragma unroll
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int ch = ch_lo; ch < ch_lo + CPW; ++ch) {
         const int c0 = tn * BN + ch * 32;
         const bool skip = (c0 >= p.N) || (r0 >= p.M) || (SYM && (c0 + 32 <= r0));
         if (!skip) todo |= 1u << ch;
@@ -895,6 +905,10 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
 #undef B2O_K
   const KernelFn fn = table[E.kind][E.d_half ? 1 : 0][sym ? 1 : 0][E.rowsq ? 1 : 0][pair - 1];
   if (!fn) { set_error("gemm: unsupported epilogue combination"); return -1; }
+  const bool ew8 = !E.rowsq;  // tc::EpiWarps
+  const int smem_bytes = pair == 1 ? (ew8 ? tc::Geo<1, 8>::SMEM_BYTES : tc::Geo<1, 4>::SMEM_BYTES)
+                                   : (ew8 ? tc::Geo<2, 8>::SMEM_BYTES : tc::Geo<2, 4>::SMEM_BYTES);
+  const int threads = ew8 ? tc::Geo<1, 8>::THREADS : tc::Geo<1, 4>::THREADS;
   static std::mutex attr_mu;
   static std::vector<std::pair<int, const void*>> configured;
   int dev = 0;
@@ -904,7 +918,7 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
     const std::pair<int, const void*> key{dev, reinterpret_cast<const void*>(fn)};
     if (std::find(configured.begin(), configured.end(), key) == configured.end()) {
       cudaError_t ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
       if (ce != cudaSuccess) { set_error(std::string("gemm: smem attribute: ") + cudaGetErrorString(ce)); return ce; }
       configured.push_back(key);
     }
@@ -913,8 +927,8 @@ int gemm(const Operand& A, const Operand& B, const Epilogue& E, int M, int N, in
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(units * pair, 1, 1);
-  cfg.blockDim = dim3(tc::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = tc::SMEM_BYTES;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

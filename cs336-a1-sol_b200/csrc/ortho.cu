@@ -15,7 +15,11 @@
 //   mode 1 (Gram Newton-Schulz): iterate on the m x m Gram matrix R = X X^T,
 //       m = min(r, c), with a per-step coefficient table:
 //       P_t = a_t I + b_t R + c_t R^2;  Q <- Q P_t;  R <- P_t R P_t
-//       and form X_T = Q X0 only at restarts and at the end. At a restart step
+//       and form X_T = Q X0 only at restarts and at the end. Between restarts
+//       R, every P_t, Q and P_t R are polynomials in one Gram matrix, hence
+//       symmetric: each m x m product computes only the tiles on or above the
+//       diagonal and mirrors them (the stored Q and R are exactly symmetric).
+//       At a restart step
 //       the iterate X = Q X0 is materialised and R recomputed from it, which
 //       bounds the drift between Q and R. The iteration runs in binary16
 //       (X0 = u/||u|| and every R, P, Q, X stay within its range; its 11-bit
@@ -145,13 +149,13 @@ __global__ void ns_normalize_kernel(const uint16_t* __restrict__ U, uint16_t* __
 // (the recipe's 8 x 1024 attention gates would otherwise take ~20 launches of
 // tiny GEMMs). Same schedule and the same binary16 rounding points as the
 // tensor-core path: X0 = f16(u * s); R = sym f16(X X^T); P = sym f16(c R^2 +
-// b R + a I); Q = f16(Q P); R <- sym f16(f16(P R) P); X1 = f16(Q X0) and
+// b R + a I); Q = sym f16(Q P); R <- sym f16(sym f16(P R) P); X1 = f16(Q X0) and
 // R = sym f16(X1 X1^T) at restarts; o = bf16(Q X) with row sums of o^2 per
 // 256-column tile. Symmetric results take the upper triangle, as the
 // tensor-core epilogue's mirror does. Accumulation is fp32.
 constexpr int kSmallM = 32;
 constexpr int kSmallElems = 49152;  // two binary16 m x n iterates in <= 192 KB of shared memory
-constexpr int kSmallThreads = 256;
+constexpr int kSmallThreads = 1024;  // 32 warps: the per-matrix phases are latency-bound
 
 struct SmallNsArgs {
   float coef[3 * 64];
@@ -263,14 +267,14 @@ __global__ void __launch_bounds__(kSmallThreads) small_gram_ns_kernel(
       for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) Q[idx] = P[idx];
       have_q = true;
     } else {
-      small_mm(Q, P, Tm, m, false, false);  // Tm = f16(Q P)
+      small_mm(Q, P, Tm, m, false, true);  // Tm = sym f16(Q P)
       __syncthreads();
       for (int idx = threadIdx.x; idx < mm; idx += blockDim.x) Q[idx] = Tm[idx];
     }
     __syncthreads();
     const bool need_r = (t < a.T - 1) && !((a.resets >> (t + 1)) & 1ull);
     if (need_r) {
-      small_mm(P, R, Tm, m, false, false);  // f16(P R)
+      small_mm(P, R, Tm, m, false, true);  // sym f16(P R)
       __syncthreads();
       small_mm(Tm, P, Rn, m, false, true);  // sym f16((P R) P)
       __syncthreads();
@@ -294,14 +298,19 @@ __global__ void __launch_bounds__(kSmallThreads) small_gram_ns_kernel(
   }
   __syncthreads();
   if (!a.tall) {
-    for (int w = threadIdx.x; w < m * a.ntn; w += blockDim.x) {
+    // one warp per (row, 256-column tile): lanes take 8 columns each, then a
+    // fixed-order shuffle reduction
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int w = warp; w < m * a.ntn; w += blockDim.x >> 5) {
       const int i = w / a.ntn, tn = w - (w / a.ntn) * a.ntn;
       float part = 0.f;
-      for (int k = tn * 256; k < min(n, tn * 256 + 256); ++k) {
+      for (int k = tn * 256 + lane; k < min(n, tn * 256 + 256); k += 32) {
         const float y = bf16_to_f32(Ob[i * n + k]);
         part = fmaf(y, y, part);
       }
-      rowsq[(static_cast<int64_t>(s) * a.ntn + tn) * a.r + i] = part;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (lane == 0) rowsq[(static_cast<int64_t>(s) * a.ntn + tn) * a.r + i] = part;
     }
   } else {
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
@@ -539,14 +548,16 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     if (Q < 0) {
       Q = P; p_owned_by_q = true;
     } else {
+      // Q and every P_t are polynomials in the Gram matrix of the last
+      // restart, so they commute and Q P_t is symmetric: upper tiles only
       const int Qn = alloc();
-      if ((rc_ = prod(ball, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
+      if ((rc_ = prod(ball, pool(Q), pool(P), epi0(pool(Qn), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
       release(Q); Q = Qn;
     }
     const bool need_r = (t < T - 1) && !is_reset(t + 1);
     if (need_r) {
-      const int T1 = alloc();
-      if ((rc_ = prod(ball, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr, 1), 0))) return rc_;
+      const int T1 = alloc();  // P R is symmetric for the same reason
+      if ((rc_ = prod(ball, pool(P), pool(R), epi0(pool(T1), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
       const int Rn = alloc();
       if ((rc_ = prod(ball, pool(T1), pool(P), epi0(pool(Rn), 0, 0, 1.0f, nullptr, 1), 1))) return rc_;
       release(T1); release(R); R = Rn;
