@@ -28,6 +28,11 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
                   uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
                   float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
                   float w_beta2, float ema_weight, float* scratch, cudaStream_t stream);
+int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                        int nesterov, cudaStream_t stream);
+int normuon_apply_multi(const b2o_normuon_batch* batches, int nb, int param_dtype, float neg_lr, float lr_wd,
+                        float wd_factor, int wd_on, int cautious, float w_beta2, float ema_weight,
+                        cudaStream_t stream);
 int64_t normuon_apply_static_max_floats();
 int normuon_apply_static(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
                          uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,

@@ -181,6 +181,19 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
                        static_cast<cudaStream_t>(stream));
 }
 
+int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small,
+                            float w_large, int nesterov, void* stream) {
+  return normuon_front_multi(batches, nbatches, dtype, w_small, w_large, nesterov,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int param_dtype, float neg_lr,
+                            float lr_wd, float wd_factor, int wd_on, int cautious, float w_beta2, float ema_weight,
+                            void* stream) {
+  return normuon_apply_multi(batches, nbatches, param_dtype, neg_lr, lr_wd, wd_factor, wd_on, cautious, w_beta2,
+                             ema_weight, static_cast<cudaStream_t>(stream));
+}
+
 int64_t b2o_normuon_apply_static_max_floats(void) { return normuon_apply_static_max_floats(); }
 
 int b2o_normuon_apply_static(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c, void* const* params,

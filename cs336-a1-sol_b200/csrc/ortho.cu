@@ -104,15 +104,41 @@ __global__ void norm_finalize_kernel(const float* __restrict__ partial, int npar
   }
 }
 
-// X0 = binary16(u * scale[s]): the normalised Gram-iteration input.
-__global__ void to_half_scaled_kernel(const uint16_t* __restrict__ U, uint16_t* __restrict__ X, int64_t rc,
-                                      const float* __restrict__ scale) {
+// Gram mode: X0 = binary16(u * s) for every matrix of every group of a
+// multi-group call in one launch; each CTA derives its matrix's scale
+// s = 1 / (||u|| * safety + eps) from the front's partial sums (summed in the
+// order norm_finalize_kernel uses).
+constexpr int kToHalfGroups = 16;
+struct ToHalfGroup {
+  const uint16_t* U;
+  uint16_t* X;
+  const float* partial;
+  int64_t rc;
+  int nparts, s0;  // s0: first matrix of the group in the launch's y range
+};
+struct ToHalfTable {
+  int ng;
+  ToHalfGroup g[kToHalfGroups];
+};
+
+__global__ void to_half_multi_kernel(const __grid_constant__ ToHalfTable t, float eps, float safety) {
   pdl_wait();
-  const int s = blockIdx.y;
-  const float sc = scale[s];
-  const uint16_t* u = U + static_cast<int64_t>(s) * rc;
-  uint16_t* x = X + static_cast<int64_t>(s) * rc;
-  const int64_t nvec = (rc % 8 == 0) ? rc / 8 : 0;  // 16-byte vectors only when every matrix is aligned
+  int gi = 0;
+  while (gi + 1 < t.ng && static_cast<int>(blockIdx.y) >= t.g[gi + 1].s0) ++gi;
+  const ToHalfGroup& G = t.g[gi];
+  const int s = blockIdx.y - G.s0;
+  __shared__ float sc_sh;
+  if (threadIdx.x == 0) {
+    float acc = 0.f;
+    for (int i = 0; i < G.nparts; ++i) acc += G.partial[static_cast<int64_t>(s) * G.nparts + i];
+    sc_sh = 1.0f / (sqrtf(acc) * safety + eps);
+  }
+  __syncthreads();
+  const float sc = sc_sh;
+  const int64_t rc = G.rc;
+  const uint16_t* u = G.U + static_cast<int64_t>(s) * rc;
+  uint16_t* x = G.X + static_cast<int64_t>(s) * rc;
+  const int64_t nvec = (rc % 8 == 0) ? rc / 8 : 0;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     uint4 in = reinterpret_cast<const uint4*>(u)[v];
@@ -451,7 +477,7 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     }
     return 0;
   }
-  for (int g = 0; g < ng; ++g) {
+  for (int g = 0; g < ng && mode == 0; ++g) {
     const int nparts = normuon_front_parts(bg[g].rc);
     launch_pdl(norm_finalize_kernel, dim3((bg[g].S + 127) / 128), dim3(128), 0, stream, groups[g].partial, nparts,
                bg[g].S, mode, norm_eps, norm_safety, scal, L.Stot, L.s_off[g]);
@@ -511,15 +537,24 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   // binary16: R, P and Q are bounded, and its 11-bit significand keeps the
   // Gram matrix far more accurate than bfloat16 at the same tensor-core rate)
   std::vector<const uint16_t*> Xcur(ng);
-  for (int g = 0; g < ng; ++g) {
-    const int64_t rc = bg[g].rc;
-    const int S = bg[g].S;
-    const int gx = static_cast<int>(std::min<int64_t>((rc / 8 + 255) / 256 + 1, std::max(1, num_sms() * 8 / S)));
-    launch_pdl(to_half_scaled_kernel, dim3(gx, S), dim3(256), 0, stream, groups[g].U, xa(g), rc,
-               static_cast<const float*>(scal + L.s_off[g]));
+  for (int g0 = 0; g0 < ng; g0 += kToHalfGroups) {
+    ToHalfTable tt;
+    memset(&tt, 0, sizeof(tt));
+    tt.ng = std::min(kToHalfGroups, ng - g0);
+    int ymats = 0;
+    int64_t max_rc = 0;
+    for (int i = 0; i < tt.ng; ++i) {
+      const int g = g0 + i;
+      tt.g[i] = ToHalfGroup{groups[g].U, xa(g), groups[g].partial, bg[g].rc, normuon_front_parts(bg[g].rc), ymats};
+      ymats += bg[g].S;
+      max_rc = std::max(max_rc, bg[g].rc);
+      Xcur[g] = xa(g);
+    }
+    const int gx = static_cast<int>(std::min<int64_t>((max_rc / 8 + 255) / 256 + 1,
+                                                      std::max(1, num_sms() * 8 / ymats)));
+    launch_pdl(to_half_multi_kernel, dim3(gx, ymats), dim3(256), 0, stream, tt, norm_eps, norm_safety);
     count_launch();
-    if (int e = check_launch("to_half_scaled")) return e;
-    Xcur[g] = xa(g);
+    if (int e = check_launch("to_half_multi")) return e;
   }
   int R = alloc();
   for (int g = 0; g < ng; ++g)

@@ -351,102 +351,184 @@ int ema_copy_to_params(const float* const* shadows, void* const* params, const i
 }
 
 // ======================================================= NorMuon front ===
-constexpr int kMaxBatch = 64;          // matrices per NorMuon launch
+// Every kernel of the NorMuon pass takes all shape batches of one parameter
+// group at once (one launch each for front, finish and apply, instead of one
+// per batch): a CTA finds its batch in a small prefix table and its matrix and
+// 8192/16384-element part inside it.
+constexpr int kMaxBatch = 64;          // matrices per batch (orthogonaliser kernel tables)
+constexpr int kMaxMultiMats = 128;     // matrices per multi-batch launch
+constexpr int kMaxMultiBatches = 16;   // batches per multi-batch launch
 constexpr int kFrontThreads = 256;
 constexpr int kFrontPart = kFrontThreads * 8 * 8;  // elements per partial sum
-
-struct FrontTable {
-  const void* g[kMaxBatch];
-  void* buf[kMaxBatch];
-};
+constexpr int kApplyThreads = 256;
+constexpr int64_t kApplyPart = kApplyThreads * 8 * 4;  // elements per apply CTA
 
 int normuon_front_parts(int64_t rc) { return static_cast<int>((rc + kFrontPart - 1) / kFrontPart); }
 
+struct MultiBatchInfo {
+  int64_t rc;
+  int r, c, S, nparts;   // nparts: CTAs per matrix
+  int mat0;              // index of the batch's first matrix in the pointer tables
+  int cta0;              // first CTA of the batch
+  int vec_ok, has_rem, has_ema;
+  float shape_scale;
+  uint16_t* u;           // front output / apply input o
+  float* partial;        // front: norm partials; apply: scratch (S * (r + 4))
+  const float* rowsq;    // apply: [S][ceil(c/256)][r]
+};
+struct MultiHeader {
+  int nb;
+  MultiBatchInfo b[kMaxMultiBatches];
+};
+
+// batch of CTA `cta` (batches are ordered by cta0)
+__device__ __forceinline__ int find_batch_cta(const MultiHeader& h, int cta) {
+  int k = 0;
+  while (k + 1 < h.nb && cta >= h.b[k + 1].cta0) ++k;
+  return k;
+}
+
+struct FrontTable {
+  MultiHeader h;
+  const void* g[kMaxMultiMats];
+  void* buf[kMaxMultiMats];
+};
+
 template <typename T>
-__global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(
-    const __grid_constant__ FrontTable tab, int64_t rc, int nparts, float w_small, float w_large,
-    int nesterov, int vec_ok, uint16_t* __restrict__ U, float* __restrict__ partial) {
+__global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __grid_constant__ FrontTable tab,
+                                                                      float w_small, float w_large, int nesterov) {
   pdl_wait();
-  const int s = blockIdx.y;
-  const T* G = reinterpret_cast<const T*>(tab.g[s]);
-  T* B = reinterpret_cast<T*>(tab.buf[s]);
-  uint16_t* Us = U + static_cast<int64_t>(s) * rc;
-  float acc = 0.f;
-  for (int part = blockIdx.x; part < nparts; part += gridDim.x) {
-    const int64_t base = static_cast<int64_t>(part) * kFrontPart;
-    const int64_t end = min(rc, base + kFrontPart);
-    float pacc = 0.f;
-    int64_t scalar_from = base;
-    if (vec_ok) {
-      for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += kFrontThreads * 8) {
-        float g[8], b[8], u[8];
-        Elem<T>::load8(G + i, g);
-        Elem<T>::load8(B + i, b);
+  const MultiBatchInfo& bi = tab.h.b[find_batch_cta(tab.h, blockIdx.x)];
+  const int local = blockIdx.x - bi.cta0;
+  const int s = local / bi.nparts;
+  const int part = local - s * bi.nparts;
+  const int64_t rc = bi.rc;
+  const T* G = reinterpret_cast<const T*>(tab.g[bi.mat0 + s]);
+  T* B = reinterpret_cast<T*>(tab.buf[bi.mat0 + s]);
+  uint16_t* Us = bi.u + static_cast<int64_t>(s) * rc;
+  const int64_t base = static_cast<int64_t>(part) * kFrontPart;
+  const int64_t end = min(rc, base + kFrontPart);
+  float pacc = 0.f;
+  int64_t scalar_from = base;
+  if (bi.vec_ok) {
+    for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += kFrontThreads * 8) {
+      float g[8], b[8], u[8];
+      Elem<T>::load8(G + i, g);
+      Elem<T>::load8(B + i, b);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          b[k] = Elem<T>::rnd(torch_lerp(b[k], g[k], w_small));   // buf.lerp_(g, 1-beta)
-          u[k] = nesterov ? Elem<T>::rnd(torch_lerp(g[k], b[k], w_large)) : b[k];  // g.lerp(buf, beta)
-          u[k] = round_bf16(u[k]);                                 // X = u.bfloat16()
-          pacc = fmaf(u[k], u[k], pacc);
-        }
-        Elem<T>::store8(B + i, b);
-        Elem<uint16_t>::store8(Us + i, u);
+      for (int k = 0; k < 8; ++k) {
+        b[k] = Elem<T>::rnd(torch_lerp(b[k], g[k], w_small));   // buf.lerp_(g, 1-beta)
+        u[k] = nesterov ? Elem<T>::rnd(torch_lerp(g[k], b[k], w_large)) : b[k];  // g.lerp(buf, beta)
+        u[k] = round_bf16(u[k]);                                 // X = u.bfloat16()
+        pacc = fmaf(u[k], u[k], pacc);
       }
-      scalar_from = base + ((end - base) / 8) * 8;
+      Elem<T>::store8(B + i, b);
+      Elem<uint16_t>::store8(Us + i, u);
     }
-    for (int64_t i = scalar_from + threadIdx.x; i < end; i += kFrontThreads) {
-      const float g = Elem<T>::load1(G + i);
-      float b = Elem<T>::load1(B + i);
-      b = Elem<T>::rnd(torch_lerp(b, g, w_small));
-      float u = nesterov ? Elem<T>::rnd(torch_lerp(g, b, w_large)) : b;
-      u = round_bf16(u);
-      pacc = fmaf(u, u, pacc);
-      Elem<T>::store1(B + i, b);
-      Us[i] = f32_to_bf16(u);
-    }
-    // deterministic block reduction of this part
-    __shared__ float red[kFrontThreads / 32];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) pacc += __shfl_xor_sync(0xffffffffu, pacc, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = pacc;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int k = 0; k < kFrontThreads / 32; ++k) t += red[k];
-      partial[static_cast<int64_t>(s) * nparts + part] = t;
-    }
-    __syncthreads();
+    scalar_from = base + ((end - base) / 8) * 8;
   }
-  (void)acc;
+  for (int64_t i = scalar_from + threadIdx.x; i < end; i += kFrontThreads) {
+    const float g = Elem<T>::load1(G + i);
+    float b = Elem<T>::load1(B + i);
+    b = Elem<T>::rnd(torch_lerp(b, g, w_small));
+    float u = nesterov ? Elem<T>::rnd(torch_lerp(g, b, w_large)) : b;
+    u = round_bf16(u);
+    pacc = fmaf(u, u, pacc);
+    Elem<T>::store1(B + i, b);
+    Us[i] = f32_to_bf16(u);
+  }
+  // deterministic block reduction of this part
+  __shared__ float red[kFrontThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) pacc += __shfl_xor_sync(0xffffffffu, pacc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = pacc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < kFrontThreads / 32; ++k) t += red[k];
+    bi.partial[static_cast<int64_t>(s) * bi.nparts + part] = t;
+  }
+}
+
+// Checks the batch list shared by the multi-batch calls and fills the header
+// (matrix and CTA offsets); parts_of(rc) = CTAs per matrix.
+template <typename PartsFn>
+static int fill_header(const b2o_normuon_batch* batches, int nb, const char* what, PartsFn parts_of, MultiHeader& h,
+                       int& nmats, int& ncta) {
+  if (nb <= 0 || nb > kMaxMultiBatches || !batches) {
+    set_error(std::string(what) + ": 1.." + std::to_string(kMaxMultiBatches) + " batches per call");
+    return -1;
+  }
+  memset(&h, 0, sizeof(h));
+  h.nb = nb;
+  nmats = 0;
+  int64_t ctas = 0;
+  for (int k = 0; k < nb; ++k) {
+    const b2o_normuon_batch& b = batches[k];
+    if (b.S <= 0 || b.S > kMaxBatch || b.r <= 0 || b.c <= 0) {
+      set_error(std::string(what) + ": batch " + std::to_string(k) + " needs 1..64 matrices of positive shape");
+      return -1;
+    }
+    MultiBatchInfo& bi = h.b[k];
+    bi.rc = static_cast<int64_t>(b.r) * b.c;
+    bi.r = b.r; bi.c = b.c; bi.S = b.S;
+    bi.nparts = parts_of(bi.rc);
+    bi.mat0 = nmats;
+    bi.cta0 = static_cast<int>(ctas);
+    bi.shape_scale = b.shape_scale;
+    nmats += b.S;
+    ctas += static_cast<int64_t>(b.S) * bi.nparts;
+  }
+  if (nmats > kMaxMultiMats) {
+    set_error(std::string(what) + ": at most " + std::to_string(kMaxMultiMats) + " matrices per call");
+    return -1;
+  }
+  if (ctas > (1ll << 30)) { set_error(std::string(what) + ": too many elements"); return -1; }
+  ncta = static_cast<int>(ctas);
+  return 0;
+}
+
+int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                        int nesterov, cudaStream_t stream) {
+  if (dtype != B2O_F32 && dtype != B2O_BF16) { set_error("normuon_front: bad dtype"); return -1; }
+  FrontTable tab;
+  int nmats = 0, ncta = 0;
+  if (int e = fill_header(batches, nb, "normuon_front", normuon_front_parts, tab.h, nmats, ncta)) return e;
+  memset(tab.g, 0, sizeof(tab.g));
+  memset(tab.buf, 0, sizeof(tab.buf));
+  for (int k = 0; k < nb; ++k) {
+    const b2o_normuon_batch& b = batches[k];
+    MultiBatchInfo& bi = tab.h.b[k];
+    if (!b.grads || !b.bufs || !b.u || !b.partial) { set_error("normuon_front: bad args"); return -1; }
+    int vec_ok = aligned16(b.u) && ((bi.rc * 2) % 16 == 0);
+    for (int s = 0; s < b.S; ++s) {
+      if (!b.grads[s] || !b.bufs[s]) { set_error("normuon_front: null matrix pointer"); return -1; }
+      tab.g[bi.mat0 + s] = b.grads[s];
+      tab.buf[bi.mat0 + s] = b.bufs[s];
+      vec_ok = vec_ok && aligned16(b.grads[s]) && aligned16(b.bufs[s]);
+    }
+    bi.vec_ok = vec_ok;
+    bi.u = b.u;
+    bi.partial = b.partial;
+  }
+  if (dtype == B2O_F32)
+    launch_pdl(normuon_front_kernel<float>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small, w_large,
+               nesterov);
+  else
+    launch_pdl(normuon_front_kernel<uint16_t>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small,
+               w_large, nesterov);
+  count_launch();
+  return check_launch("normuon_front");
 }
 
 int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int c, int dtype,
                   float w_small, float w_large, int nesterov, uint16_t* U, float* partial,
                   cudaStream_t stream) {
-  if (S <= 0 || S > kMaxBatch) { set_error("normuon_front: 1..64 matrices per batch"); return -1; }
-  if (r <= 0 || c <= 0 || !grads || !bufs || !U || !partial) { set_error("normuon_front: bad args"); return -1; }
-  if (dtype != B2O_F32 && dtype != B2O_BF16) { set_error("normuon_front: bad dtype"); return -1; }
-  FrontTable tab;
-  memset(&tab, 0, sizeof(tab));
-  int vec_ok = aligned16(U);
-  const int64_t rc = static_cast<int64_t>(r) * c;
-  if ((rc * 2) % 16) vec_ok = 0;
-  for (int s = 0; s < S; ++s) {
-    if (!grads[s] || !bufs[s]) { set_error("normuon_front: null matrix pointer"); return -1; }
-    tab.g[s] = grads[s];
-    tab.buf[s] = bufs[s];
-    vec_ok = vec_ok && aligned16(grads[s]) && aligned16(bufs[s]);
-  }
-  const int nparts = normuon_front_parts(rc);
-  dim3 grid(nparts, S);
-  if (dtype == B2O_F32)
-    launch_pdl(normuon_front_kernel<float>, grid, dim3(kFrontThreads), 0, stream, tab, rc, nparts, w_small,
-               w_large, nesterov, vec_ok, U, partial);
-  else
-    launch_pdl(normuon_front_kernel<uint16_t>, grid, dim3(kFrontThreads), 0, stream, tab, rc, nparts, w_small,
-               w_large, nesterov, vec_ok, U, partial);
-  count_launch();
-  return check_launch("normuon_front");
+  b2o_normuon_batch b;
+  memset(&b, 0, sizeof(b));
+  b.S = S; b.r = r; b.c = c;
+  b.grads = grads; b.bufs = bufs; b.u = U; b.partial = partial;
+  return normuon_front_multi(&b, 1, dtype, w_small, w_large, nesterov, stream);
 }
 
 // ====================================================== NorMuon finish ===
@@ -454,7 +536,10 @@ int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int
 // row sums, updates v_row (sol_modules.py:398) and produces the per-row factor
 // 1/(sqrt(v_row)+1e-10) (:399) and the per-matrix norm-restoring factor
 // vnorm/(||o*inv||+1e-10) (:397, :400).
-struct VrowTable { float* v[kMaxBatch]; };
+struct FinishTable {
+  MultiHeader h;
+  float* v[kMaxMultiMats];
+};
 
 __device__ float block_sum_1024(float x, float* red) {
 #pragma unroll
@@ -472,15 +557,19 @@ __device__ float block_sum_1024(float x, float* red) {
   return t;
 }
 
-__global__ void __launch_bounds__(1024) normuon_finish_kernel(
-    const __grid_constant__ VrowTable vt, const float* __restrict__ rowsq, int r, int c, int ntn,
-    float w_beta2, float* __restrict__ scratch) {
+__global__ void __launch_bounds__(1024) normuon_finish_kernel(const __grid_constant__ FinishTable tab,
+                                                              float w_beta2) {
   pdl_wait();
   __shared__ float red[33];
-  const int s = blockIdx.x;
-  float* inv = scratch + static_cast<int64_t>(s) * (r + 4);
-  const float* part = rowsq + static_cast<int64_t>(s) * ntn * r;
-  float* vrow = vt.v[s];
+  // one CTA per matrix: the batch is the last one whose first matrix is <= blockIdx.x
+  int k = 0;
+  while (k + 1 < tab.h.nb && static_cast<int>(blockIdx.x) >= tab.h.b[k + 1].mat0) ++k;
+  const MultiBatchInfo& bi = tab.h.b[k];
+  const int s = blockIdx.x - bi.mat0;
+  const int r = bi.r, c = bi.c, ntn = (c + 255) / 256;
+  float* inv = bi.partial + static_cast<int64_t>(s) * (r + 4);
+  const float* part = bi.rowsq + static_cast<int64_t>(s) * ntn * r;
+  float* vrow = tab.v[blockIdx.x];
   float sumsq = 0.f, n1 = 0.f;
   for (int i = threadIdx.x; i < r; i += blockDim.x) {
     float rs = 0.f;
@@ -500,15 +589,15 @@ __global__ void __launch_bounds__(1024) normuon_finish_kernel(
 
 // ======================================================= NorMuon apply ===
 struct ApplyTable {
-  void* p[kMaxBatch];
-  uint16_t* rem[kMaxBatch];
-  float* ema[kMaxBatch];
+  MultiHeader h;
+  void* p[kMaxMultiMats];
+  uint16_t* rem[kMaxMultiMats];
+  float* ema[kMaxMultiMats];
 };
 
 struct ApplyArgs {
-  int64_t rc;
-  int r, c, nparts, has_rem, has_ema, wd_on, cautious, vec_ok;
-  float neg_lr, lr_wd, wd_factor, shape_scale, ema_w;
+  int wd_on, cautious;
+  float neg_lr, lr_wd, wd_factor, ema_w;
 };
 
 // mode: 0 = fp32 params; 1 = bf16 params with remainder (bf16_master);
@@ -540,118 +629,141 @@ __device__ __forceinline__ void apply_elem(const ApplyArgs& a, float o3, float& 
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(256) normuon_apply_kernel(
-    const __grid_constant__ ApplyTable tab, const __grid_constant__ ApplyArgs a,
-    const uint16_t* __restrict__ O, const float* __restrict__ scratch) {
+__global__ void __launch_bounds__(kApplyThreads) normuon_apply_kernel(const __grid_constant__ ApplyTable tab,
+                                                                      const __grid_constant__ ApplyArgs a) {
   pdl_wait();
-  const int s = blockIdx.y;
-  const float* inv = scratch + static_cast<int64_t>(s) * (a.r + 4);
-  const float f = inv[a.r];
-  const uint16_t* Os = O + static_cast<int64_t>(s) * a.rc;
-  float* E = a.has_ema ? tab.ema[s] : nullptr;
-  uint16_t* R = a.has_rem ? tab.rem[s] : nullptr;
+  const MultiBatchInfo& bi = tab.h.b[find_batch_cta(tab.h, blockIdx.x)];
+  const int local = blockIdx.x - bi.cta0;
+  const int s = local / bi.nparts;
+  const int part = local - s * bi.nparts;
+  const int64_t rc = bi.rc;
+  const int c = bi.c;
+  const float* inv = bi.partial + static_cast<int64_t>(s) * (bi.r + 4);
+  const float f = inv[bi.r];
+  const float sscale = bi.shape_scale;
+  const uint16_t* Os = bi.u + static_cast<int64_t>(s) * rc;
+  float* E = bi.has_ema ? tab.ema[bi.mat0 + s] : nullptr;
+  uint16_t* R = bi.has_rem ? tab.rem[bi.mat0 + s] : nullptr;
   using PT = typename std::conditional<MODE == 0, float, uint16_t>::type;
-  PT* P = reinterpret_cast<PT*>(tab.p[s]);
-  const int64_t per_part = 256 * 8 * 4;
-  for (int part = blockIdx.x; part * per_part < a.rc; part += gridDim.x) {
-    const int64_t base = static_cast<int64_t>(part) * per_part;
-    const int64_t end = min(a.rc, base + per_part);
-    int64_t scalar_from = base;
-    if (a.vec_ok) {
-      for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += 256 * 8) {
-        float o[8], w[8], rm[8];
-        Elem<uint16_t>::load8(Os + i, o);
-        Elem<PT>::load8(P + i, w);
-        if (MODE == 1) {
-          float r0[8];
-          Elem<uint16_t>::load8(R + i, r0);
+  PT* P = reinterpret_cast<PT*>(tab.p[bi.mat0 + s]);
+  const int64_t base = static_cast<int64_t>(part) * kApplyPart;
+  const int64_t end = min(rc, base + kApplyPart);
+  int64_t scalar_from = base;
+  if (bi.vec_ok) {
+    for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += kApplyThreads * 8) {
+      float o[8], w[8], rm[8];
+      Elem<uint16_t>::load8(Os + i, o);
+      Elem<PT>::load8(P + i, w);
+      if (MODE == 1) {
+        float r0[8];
+        Elem<uint16_t>::load8(R + i, r0);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) w[k] = w[k] + r0[k];
-        }
-        // 8 consecutive elements may straddle a row boundary when c % 8 != 0
-        // (excluded by vec_ok), so one row index serves all 8.
-        const int row = static_cast<int>(i / a.c);
-        const float iv = inv[row];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float o3 = ((o[k] * iv) * f) * a.shape_scale;
-          apply_elem<MODE>(a, o3, w[k], rm[k]);
-        }
-        Elem<PT>::store8(P + i, w);
-        if (MODE == 1) Elem<uint16_t>::store8(R + i, rm);
-        if (E) {
-          float e[8];
-          Elem<float>::load8(E + i, e);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) e[k] = torch_lerp(e[k], w[k], a.ema_w);
-          Elem<float>::store8(E + i, e);
-        }
+        for (int k = 0; k < 8; ++k) w[k] = w[k] + r0[k];
       }
-      scalar_from = base + ((end - base) / 8) * 8;
+      // 8 consecutive elements may straddle a row boundary when c % 8 != 0
+      // (excluded by vec_ok), so one row index serves all 8.
+      const int row = static_cast<int>(i / c);
+      const float iv = inv[row];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float o3 = ((o[k] * iv) * f) * sscale;
+        apply_elem<MODE>(a, o3, w[k], rm[k]);
+      }
+      Elem<PT>::store8(P + i, w);
+      if (MODE == 1) Elem<uint16_t>::store8(R + i, rm);
+      if (E) {
+        float e[8];
+        Elem<float>::load8(E + i, e);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = torch_lerp(e[k], w[k], a.ema_w);
+        Elem<float>::store8(E + i, e);
+      }
     }
-    for (int64_t i = scalar_from + threadIdx.x; i < end; i += 256) {
-      float w = Elem<PT>::load1(P + i), rm = 0.f;
-      if (MODE == 1) w = w + bf16_to_f32(R[i]);
-      const int row = static_cast<int>(i / a.c);
-      const float o3 = ((bf16_to_f32(Os[i]) * inv[row]) * f) * a.shape_scale;
-      apply_elem<MODE>(a, o3, w, rm);
-      Elem<PT>::store1(P + i, w);
-      if (MODE == 1) R[i] = f32_to_bf16(rm);
-      if (E) E[i] = torch_lerp(E[i], w, a.ema_w);
-    }
+    scalar_from = base + ((end - base) / 8) * 8;
   }
+  for (int64_t i = scalar_from + threadIdx.x; i < end; i += kApplyThreads) {
+    float w = Elem<PT>::load1(P + i), rm = 0.f;
+    if (MODE == 1) w = w + bf16_to_f32(R[i]);
+    const int row = static_cast<int>(i / c);
+    const float o3 = ((bf16_to_f32(Os[i]) * inv[row]) * f) * sscale;
+    apply_elem<MODE>(a, o3, w, rm);
+    Elem<PT>::store1(P + i, w);
+    if (MODE == 1) R[i] = f32_to_bf16(rm);
+    if (E) E[i] = torch_lerp(E[i], w, a.ema_w);
+  }
+}
+
+static int apply_parts(int64_t rc) { return static_cast<int>((rc + kApplyPart - 1) / kApplyPart); }
+
+int normuon_apply_multi(const b2o_normuon_batch* batches, int nb, int param_dtype, float neg_lr, float lr_wd,
+                        float wd_factor, int wd_on, int cautious, float w_beta2, float ema_weight,
+                        cudaStream_t stream) {
+  if (param_dtype != B2O_F32 && param_dtype != B2O_BF16) { set_error("normuon_apply: bad dtype"); return -1; }
+  ApplyTable tab;
+  int nmats = 0, ncta = 0;
+  if (int e = fill_header(batches, nb, "normuon_apply", apply_parts, tab.h, nmats, ncta)) return e;
+  memset(tab.p, 0, sizeof(tab.p));
+  memset(tab.rem, 0, sizeof(tab.rem));
+  memset(tab.ema, 0, sizeof(tab.ema));
+  FinishTable ft;
+  memset(&ft, 0, sizeof(ft));
+  const bool with_rem = batches[0].rems != nullptr;
+  for (int k = 0; k < nb; ++k) {
+    const b2o_normuon_batch& b = batches[k];
+    MultiBatchInfo& bi = tab.h.b[k];
+    if (!b.o || !b.rowsq || !b.params || !b.vrows || !b.scratch) { set_error("normuon_apply: bad args"); return -1; }
+    if ((b.rems != nullptr) != with_rem) {
+      set_error("normuon_apply: every batch of one call needs a remainder, or none"); return -1;
+    }
+    if (b.rems && param_dtype != B2O_BF16) { set_error("normuon_apply: remainder needs bf16 params"); return -1; }
+    int vec_ok = (b.c % 8 == 0) && aligned16(b.o);
+    for (int s = 0; s < b.S; ++s) {
+      if (!b.params[s] || !b.vrows[s] || (b.rems && !b.rems[s]) || (b.emas && !b.emas[s])) {
+        set_error("normuon_apply: null matrix pointer"); return -1;
+      }
+      tab.p[bi.mat0 + s] = b.params[s];
+      tab.rem[bi.mat0 + s] = b.rems ? b.rems[s] : nullptr;
+      tab.ema[bi.mat0 + s] = b.emas ? b.emas[s] : nullptr;
+      ft.v[bi.mat0 + s] = b.vrows[s];
+      vec_ok = vec_ok && aligned16(b.params[s]) && (!b.rems || aligned16(b.rems[s])) &&
+               (!b.emas || aligned16(b.emas[s]));
+    }
+    bi.vec_ok = vec_ok;
+    bi.has_rem = b.rems != nullptr;
+    bi.has_ema = b.emas != nullptr;
+    bi.u = const_cast<uint16_t*>(b.o);
+    bi.partial = b.scratch;
+    bi.rowsq = b.rowsq;
+  }
+  ft.h = tab.h;
+  ApplyArgs a;
+  memset(&a, 0, sizeof(a));
+  a.wd_on = wd_on; a.cautious = cautious;
+  a.neg_lr = neg_lr; a.lr_wd = lr_wd; a.wd_factor = wd_factor; a.ema_w = ema_weight;
+  launch_pdl(normuon_finish_kernel, dim3(nmats), dim3(1024), 0, stream, ft, w_beta2);
+  count_launch();
+  if (int e = check_launch("normuon_finish")) return e;
+  if (param_dtype == B2O_F32)
+    launch_pdl(normuon_apply_kernel<0>, dim3(ncta), dim3(kApplyThreads), 0, stream, tab, a);
+  else if (with_rem)
+    launch_pdl(normuon_apply_kernel<1>, dim3(ncta), dim3(kApplyThreads), 0, stream, tab, a);
+  else
+    launch_pdl(normuon_apply_kernel<2>, dim3(ncta), dim3(kApplyThreads), 0, stream, tab, a);
+  count_launch();
+  return check_launch("normuon_apply");
 }
 
 int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, void* const* params,
                   uint16_t* const* rems, float* const* emas, float* const* vrows, int param_dtype,
                   float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
                   float w_beta2, float ema_weight, float* scratch, cudaStream_t stream) {
-  if (S <= 0 || S > kMaxBatch) { set_error("normuon_apply: 1..64 matrices per batch"); return -1; }
-  if (r <= 0 || c <= 0 || !O || !rowsq || !params || !vrows || !scratch) {
-    set_error("normuon_apply: bad args"); return -1;
-  }
-  if (param_dtype != B2O_F32 && param_dtype != B2O_BF16) { set_error("normuon_apply: bad dtype"); return -1; }
-  if (rems && param_dtype != B2O_BF16) { set_error("normuon_apply: remainder needs bf16 params"); return -1; }
-  VrowTable vt;
-  memset(&vt, 0, sizeof(vt));
-  ApplyTable tab;
-  memset(&tab, 0, sizeof(tab));
-  ApplyArgs a;
-  memset(&a, 0, sizeof(a));
-  a.rc = static_cast<int64_t>(r) * c;
-  a.r = r; a.c = c;
-  a.has_rem = rems != nullptr;
-  a.has_ema = emas != nullptr;
-  a.wd_on = wd_on; a.cautious = cautious;
-  a.neg_lr = neg_lr; a.lr_wd = lr_wd; a.wd_factor = wd_factor; a.shape_scale = shape_scale; a.ema_w = ema_weight;
-  int vec_ok = (c % 8 == 0) && aligned16(O);
-  for (int s = 0; s < S; ++s) {
-    if (!params[s] || !vrows[s] || (rems && !rems[s]) || (emas && !emas[s])) {
-      set_error("normuon_apply: null matrix pointer"); return -1;
-    }
-    tab.p[s] = params[s];
-    tab.rem[s] = rems ? rems[s] : nullptr;
-    tab.ema[s] = emas ? emas[s] : nullptr;
-    vt.v[s] = vrows[s];
-    vec_ok = vec_ok && aligned16(params[s]) && (!rems || aligned16(rems[s])) && (!emas || aligned16(emas[s]));
-  }
-  a.vec_ok = vec_ok;
-  const int ntn = (c + 255) / 256;
-  launch_pdl(normuon_finish_kernel, dim3(S), dim3(1024), 0, stream, vt, rowsq, r, c, ntn, w_beta2, scratch);
-  count_launch();
-  if (int e = check_launch("normuon_finish")) return e;
-  const int64_t per_part = 256 * 8 * 4;
-  const int parts = static_cast<int>((a.rc + per_part - 1) / per_part);
-  const int gx = std::max(1, std::min(parts, (num_sms() * 8 + S - 1) / S));
-  dim3 grid(gx, S);
-  if (param_dtype == B2O_F32)
-    launch_pdl(normuon_apply_kernel<0>, grid, dim3(256), 0, stream, tab, a, O, scratch);
-  else if (rems)
-    launch_pdl(normuon_apply_kernel<1>, grid, dim3(256), 0, stream, tab, a, O, scratch);
-  else
-    launch_pdl(normuon_apply_kernel<2>, grid, dim3(256), 0, stream, tab, a, O, scratch);
-  count_launch();
-  return check_launch("normuon_apply");
+  b2o_normuon_batch b;
+  memset(&b, 0, sizeof(b));
+  b.S = S; b.r = r; b.c = c;
+  b.o = O; b.rowsq = rowsq; b.params = params; b.rems = rems; b.emas = emas; b.vrows = vrows;
+  b.shape_scale = shape_scale; b.scratch = scratch;
+  return normuon_apply_multi(&b, 1, param_dtype, neg_lr, lr_wd, wd_factor, wd_on, cautious, w_beta2, ema_weight,
+                             stream);
 }
 
 // ----------------------------------------------- allocation-free variant ---

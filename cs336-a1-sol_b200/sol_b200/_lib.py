@@ -51,6 +51,27 @@ class AdamwGroup(C.Structure):
     ]
 
 
+class NormuonBatch(C.Structure):
+    """b2o_normuon_batch: one shape batch of a multi-batch front/apply call."""
+    _fields_ = [
+        ("S", C.c_int32),
+        ("r", C.c_int32),
+        ("c", C.c_int32),
+        ("shape_scale", C.c_float),
+        ("grads", c_void_p),
+        ("bufs", c_void_p),
+        ("u", c_void_p),
+        ("partial", c_void_p),
+        ("o", c_void_p),
+        ("rowsq", c_void_p),
+        ("params", c_void_p),
+        ("rems", c_void_p),
+        ("emas", c_void_p),
+        ("vrows", c_void_p),
+        ("scratch", c_void_p),
+    ]
+
+
 class OrthoGroup(C.Structure):
     _fields_ = [
         ("u", c_void_p),
@@ -107,6 +128,9 @@ SIGNATURES = {
     "b2o_gemm_bf16_simt": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
                                    c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
+    "b2o_normuon_front_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_int, c_void_p]),
+    "b2o_normuon_apply_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_float, c_int,
+                                        c_int, c_float, c_float, c_void_p]),
     "b2o_ipc_export": (c_int, [c_void_p, c_void_p, C.POINTER(C.c_uint64)]),
     "b2o_ipc_import": (c_int, [c_void_p, C.POINTER(c_void_p)]),
     "b2o_ipc_close": (c_int, [c_void_p]),
@@ -160,6 +184,11 @@ def stream_ptr(device: torch.device | None = None) -> int:
 
 def ptr_array(ptrs) -> C.Array:
     return (c_void_p * len(ptrs))(*[int(x) if x else None for x in ptrs])
+
+
+def addr(arr) -> int | None:
+    """Address of a ctypes array (for pointer fields of a struct), or None."""
+    return C.addressof(arr) if arr is not None else None
 
 
 def dtype_code(dt: torch.dtype) -> int:

@@ -6,14 +6,17 @@ same constructor arguments, param-group keys, per-parameter state
 (r, c) when ``bf16_master`` and the param is bf16) and the overridable
 ``_orthogonalize_batch(U, ns_steps)`` hook (:366).
 
-Per exact-shape batch (the reference buckets by ``tuple(p.shape)``, :380-383)
-one step is three library calls, with no stacking copies:
+Matrices are batched by exact shape (the reference buckets by
+``tuple(p.shape)``, :380-383); one step is three kinds of library calls, with
+no stacking copies:
   front  (momentum lerp + Nesterov, :390-394)  -> u (S, r, c) bf16 + norm partials
   orthogonalise (:395; GEMMs on tcgen05)       -> o (S, r, c) bf16 + row sums of o^2
   finish + apply (v_row lerp, scale factors, cautious WD, update, bf16
          mantissa split, EMA; :396-424).
-The orthogonalisation of all batches that share m = min(r, c) is one call, so
-their m x m products run as single batched GEMMs.
+The front and the finish + apply passes cover every batch of a parameter group
+in one call each (one launch, resp. two); the orthogonalisation of all
+batches that share m = min(r, c) is one call, so their m x m products run as
+single batched GEMMs.
 """
 from __future__ import annotations
 
@@ -142,9 +145,8 @@ class NorMuonGNS(torch.optim.Optimizer):
             st["mant_rem"] = torch.zeros_like(p)
         return st
 
-    def _front(self, params, shape, group):
-        """Momentum + Nesterov for one exact-shape batch; returns the batch record."""
-        lib = _lib.load()
+    def _prepare(self, params, shape, group):
+        """Validates one exact-shape batch and returns its record (state, workspace)."""
         p0 = params[0]
         _lib.require_cuda(p0, "NorMuonGNS.step")
         dev = p0.device
@@ -157,14 +159,42 @@ class NorMuonGNS(torch.optim.Optimizer):
                 raise ValueError("NorMuonGNS needs contiguous params and grads of the param dtype")
         states = [self._init_state(p) for p in params]
         ws = self._workspace(dev, S, r, c)
-        beta = float(group["momentum"])
-        grads = _lib.ptr_array([p.grad.data_ptr() for p in params])
-        bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in states])
-        rc = lib.b2o_normuon_front(grads, bufs, S, r, c, _lib.dtype_code(p0.dtype), 1.0 - beta, beta,
-                                   int(bool(group["nesterov"])), ws["u"].data_ptr(), ws["partial"].data_ptr(),
-                                   _lib.stream_ptr(dev))
-        _lib.check(rc, "normuon_front")
         return dict(params=params, states=states, ws=ws, S=S, r=r, c=c, dev=dev, o=ws["o"])
+
+    @staticmethod
+    def _calls(recs, key):
+        """Splits batch records into library calls: same key, <= 16 batches, <= 128 matrices."""
+        calls = OrderedDict()
+        for b in recs:
+            calls.setdefault(key(b), []).append(b)
+        for k, members in calls.items():
+            cur, mats = [], 0
+            for b in members:
+                if cur and (len(cur) == 16 or mats + b["S"] > 128):
+                    yield k, cur
+                    cur, mats = [], 0
+                cur.append(b)
+                mats += b["S"]
+            if cur:
+                yield k, cur
+
+    def _front_all(self, recs, group):
+        """Momentum + Nesterov (sol_modules.py:390-394) for every batch: one launch per call."""
+        lib = _lib.load()
+        beta = float(group["momentum"])
+        for (dev, dt), members in self._calls(recs, lambda b: (b["dev"], b["params"][0].dtype)):
+            arr = (_lib.NormuonBatch * len(members))()
+            keep = []
+            for i, b in enumerate(members):
+                grads = _lib.ptr_array([p.grad.data_ptr() for p in b["params"]])
+                bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in b["states"]])
+                keep += [grads, bufs]
+                arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"], grads=_lib.addr(grads),
+                                           bufs=_lib.addr(bufs), u=b["ws"]["u"].data_ptr(),
+                                           partial=b["ws"]["partial"].data_ptr())
+            rc = lib.b2o_normuon_front_multi(arr, len(members), _lib.dtype_code(dt), 1.0 - beta, beta,
+                                             int(bool(group["nesterov"])), _lib.stream_ptr(dev))
+            _lib.check(rc, "normuon_front")
 
     def _ortho_class(self, batches, ns_steps):
         """Orthogonalises every batch of one m = min(r, c) class with one library call."""
@@ -192,35 +222,47 @@ class NorMuonGNS(torch.optim.Optimizer):
             e1.record()
             ev.append((e0, e1))
 
-    def _apply(self, b, group):
+    def _apply_all(self, recs, group):
+        """v_row, normalisation, shape scale, cautious WD, update, mantissa split and
+        EMA (sol_modules.py:396-424) for every batch: two launches per call."""
         lib = _lib.load()
-        params, states, ws = b["params"], b["states"], b["ws"]
-        S, r, c, dev = b["S"], b["r"], b["c"], b["dev"]
-        p0 = params[0]
         beta2 = float(group["beta2"])
         lr, wd = float(group["lr"]), float(group["weight_decay"])
-        mt = self.bf16_master and p0.dtype == torch.bfloat16
-        pptr = _lib.ptr_array([p.data_ptr() for p in params])
-        rems = _lib.ptr_array([st["mant_rem"].data_ptr() for st in states]) if mt else None
-        vrows = _lib.ptr_array([st["v_row"].data_ptr() for st in states])
-        emas = None
-        if self._ema is not None:
-            shadows = [self._ema._lookup(p) for p in params]
-            if all(s is not None for s in shadows):
-                emas = _lib.ptr_array([s.data_ptr() for s in shadows])
-                for p in params:
-                    self._ema._mark(p)
-        wd_on = 1 if wd else 0
-        shape_scale = math.sqrt(max(1.0, r / c))
-        rc = lib.b2o_normuon_apply(b["o"].data_ptr(), ws["rowsq"].data_ptr(), S, r, c, pptr, rems, emas, vrows,
-                                   _lib.dtype_code(p0.dtype), -lr, lr * wd, 1.0 - lr * wd, wd_on,
-                                   int(bool(self.cautious_wd and wd)), shape_scale, 1.0 - beta2, self._ema_weight,
-                                   ws["scratch"].data_ptr(), _lib.stream_ptr(dev))
-        _lib.check(rc, "normuon_apply")
+
+        def key(b):
+            p0 = b["params"][0]
+            return (b["dev"], p0.dtype, bool(self.bf16_master and p0.dtype == torch.bfloat16))
+
+        for (dev, dt, mt), members in self._calls(recs, key):
+            arr = (_lib.NormuonBatch * len(members))()
+            keep = []
+            for i, b in enumerate(members):
+                params, states, ws = b["params"], b["states"], b["ws"]
+                pptr = _lib.ptr_array([p.data_ptr() for p in params])
+                rems = _lib.ptr_array([st["mant_rem"].data_ptr() for st in states]) if mt else None
+                vrows = _lib.ptr_array([st["v_row"].data_ptr() for st in states])
+                emas = None
+                if self._ema is not None:
+                    shadows = [self._ema._lookup(p) for p in params]
+                    if all(s is not None for s in shadows):
+                        emas = _lib.ptr_array([s.data_ptr() for s in shadows])
+                        for p in params:
+                            self._ema._mark(p)
+                keep += [pptr, rems, vrows, emas]
+                arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"],
+                                           shape_scale=math.sqrt(max(1.0, b["r"] / b["c"])),
+                                           o=b["o"].data_ptr(), rowsq=ws["rowsq"].data_ptr(),
+                                           params=_lib.addr(pptr), rems=_lib.addr(rems), emas=_lib.addr(emas),
+                                           vrows=_lib.addr(vrows), scratch=ws["scratch"].data_ptr())
+            rc = lib.b2o_normuon_apply_multi(arr, len(members), _lib.dtype_code(dt), -lr, lr * wd, 1.0 - lr * wd,
+                                             1 if wd else 0, int(bool(self.cautious_wd and wd)), 1.0 - beta2,
+                                             self._ema_weight, _lib.stream_ptr(dev))
+            _lib.check(rc, "normuon_apply")
 
     def _step_group(self, batches, group):
         ns_steps = int(group["ns_steps"])
-        recs = [self._front(params, shape, group) for shape, params in batches]
+        recs = [self._prepare(params, shape, group) for shape, params in batches]
+        self._front_all(recs, group)
         if self._hook_overridden():
             for b in recs:
                 S, r, c = b["S"], b["r"], b["c"]
@@ -236,8 +278,7 @@ class NorMuonGNS(torch.optim.Optimizer):
                 classes.setdefault((b["dev"], min(b["r"], b["c"])), []).append(b)
             for members in classes.values():
                 self._ortho_class(members, ns_steps)
-        for b in recs:
-            self._apply(b, group)
+        self._apply_all(recs, group)
 
     @torch.no_grad()
     def step(self, closure=None):

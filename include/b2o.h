@@ -169,6 +169,33 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
                       float shape_scale, float w_beta2, float ema_weight,
                       float* d_scratch, void* stream);
 
+/* All shape batches of one NorMuon parameter group in one call each (one
+ * launch for the front, one each for the finish and apply passes, instead of
+ * one per batch). Same per-matrix arithmetic as b2o_normuon_front and
+ * b2o_normuon_apply; the reference's per-shape loop is
+ * transformer_lm/sol_modules.py:380-424. Up to 16 batches and 128 matrices
+ * per call; the apply call needs a remainder for every batch or for none. */
+typedef struct b2o_normuon_batch {
+  int S, r, c;                  /* S matrices of r x c */
+  float shape_scale;            /* apply: sqrt(max(1, r / c)) (sol_modules.py:401) */
+  const void* const* grads;     /* front: S gradients (param dtype) */
+  void* const* bufs;            /* front: S momentum buffers */
+  uint16_t* u;                  /* front output: S*r*c bf16 */
+  float* partial;               /* front output: S * b2o_normuon_front_parts(r*c) */
+  const uint16_t* o;            /* apply input: S*r*c bf16 orthogonaliser output */
+  const float* rowsq;           /* apply input: [S][ceil(c/256)][r] row sums of o^2 */
+  void* const* params;          /* apply: S params */
+  uint16_t* const* rems;        /* apply: S bf16 remainders, or NULL */
+  float* const* emas;           /* apply: S fp32 EMA shadows, or NULL */
+  float* const* vrows;          /* apply: S fp32 (r, 1) second moments */
+  float* scratch;               /* apply: b2o_normuon_apply_scratch_floats(S, r) floats */
+} b2o_normuon_batch;
+int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small,
+                            float w_large, int nesterov, void* stream);
+int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int param_dtype, float neg_lr,
+                            float lr_wd, float wd_factor, int wd_on, int cautious, float w_beta2,
+                            float ema_weight, void* stream);
+
 /* Allocation-free form of b2o_normuon_apply. No counterpart in the reference
  * (its optimizer allocates its temporaries through PyTorch).
  * For hosts that cannot hand the library a scratch buffer: a caller whose
