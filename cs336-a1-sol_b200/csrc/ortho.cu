@@ -109,24 +109,30 @@ __global__ void norm_finalize_kernel(const float* __restrict__ partial, int npar
 // s = 1 / (||u|| * safety + eps) from the front's partial sums (summed in the
 // order norm_finalize_kernel uses).
 constexpr int kToHalfGroups = 16;
+constexpr int64_t kToHalfPart = 256 * 8 * 16;  // elements per CTA
 struct ToHalfGroup {
   const uint16_t* U;
   uint16_t* X;
   const float* partial;
   int64_t rc;
-  int nparts, s0;  // s0: first matrix of the group in the launch's y range
+  int nparts;      // front partial sums per matrix
+  int cparts;      // CTAs per matrix
+  int cta0;        // first CTA of the group
 };
 struct ToHalfTable {
   int ng;
   ToHalfGroup g[kToHalfGroups];
 };
 
-__global__ void to_half_multi_kernel(const __grid_constant__ ToHalfTable t, float eps, float safety) {
+__global__ void __launch_bounds__(256) to_half_multi_kernel(const __grid_constant__ ToHalfTable t, float eps,
+                                                            float safety) {
   pdl_wait();
   int gi = 0;
-  while (gi + 1 < t.ng && static_cast<int>(blockIdx.y) >= t.g[gi + 1].s0) ++gi;
+  while (gi + 1 < t.ng && static_cast<int>(blockIdx.x) >= t.g[gi + 1].cta0) ++gi;
   const ToHalfGroup& G = t.g[gi];
-  const int s = blockIdx.y - G.s0;
+  const int local = blockIdx.x - G.cta0;
+  const int s = local / G.cparts;
+  const int part = local - s * G.cparts;
   __shared__ float sc_sh;
   if (threadIdx.x == 0) {
     float acc = 0.f;
@@ -138,22 +144,24 @@ __global__ void to_half_multi_kernel(const __grid_constant__ ToHalfTable t, floa
   const int64_t rc = G.rc;
   const uint16_t* u = G.U + static_cast<int64_t>(s) * rc;
   uint16_t* x = G.X + static_cast<int64_t>(s) * rc;
-  const int64_t nvec = (rc % 8 == 0) ? rc / 8 : 0;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
-       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    uint4 in = reinterpret_cast<const uint4*>(u)[v];
-    uint32_t w[4] = {in.x, in.y, in.z, in.w};
+  const int64_t base = static_cast<int64_t>(part) * kToHalfPart;
+  const int64_t end = min(rc, base + kToHalfPart);
+  int64_t scalar_from = base;
+  if (rc % 8 == 0) {  // 16-byte vectors only when every matrix is aligned
+    for (int64_t i = base + threadIdx.x * 8; i + 8 <= end; i += 256 * 8) {
+      const uint4 in = *reinterpret_cast<const uint4*>(u + i);
+      uint32_t w[4] = {in.x, in.y, in.z, in.w};
 #pragma unroll
-    for (int h = 0; h < 4; ++h) {
-      const uint16_t lo = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu)) * sc);
-      const uint16_t hi = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] >> 16)) * sc);
-      w[h] = lo | (static_cast<uint32_t>(hi) << 16);
+      for (int h = 0; h < 4; ++h) {
+        const uint16_t lo = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] & 0xFFFFu)) * sc);
+        const uint16_t hi = f32_to_f16(bf16_to_f32(static_cast<uint16_t>(w[h] >> 16)) * sc);
+        w[h] = lo | (static_cast<uint32_t>(hi) << 16);
+      }
+      *reinterpret_cast<uint4*>(x + i) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    reinterpret_cast<uint4*>(x)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+    scalar_from = base + ((end - base) / 8) * 8;
   }
-  for (int64_t i = nvec * 8 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < rc;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    x[i] = f32_to_f16(bf16_to_f32(u[i]) * sc);
+  for (int64_t i = scalar_from + threadIdx.x; i < end; i += 256) x[i] = f32_to_f16(bf16_to_f32(u[i]) * sc);
 }
 
 // X0 = bf16(u / d[s]) (the division of zeropower_via_newtonschulz5, sol_modules.py:283).
@@ -541,18 +549,18 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     ToHalfTable tt;
     memset(&tt, 0, sizeof(tt));
     tt.ng = std::min(kToHalfGroups, ng - g0);
-    int ymats = 0;
-    int64_t max_rc = 0;
+    int64_t ctas = 0;
     for (int i = 0; i < tt.ng; ++i) {
       const int g = g0 + i;
-      tt.g[i] = ToHalfGroup{groups[g].U, xa(g), groups[g].partial, bg[g].rc, normuon_front_parts(bg[g].rc), ymats};
-      ymats += bg[g].S;
-      max_rc = std::max(max_rc, bg[g].rc);
+      const int cparts = static_cast<int>((bg[g].rc + kToHalfPart - 1) / kToHalfPart);
+      tt.g[i] = ToHalfGroup{groups[g].U, xa(g), groups[g].partial, bg[g].rc, normuon_front_parts(bg[g].rc),
+                            cparts, static_cast<int>(ctas)};
+      ctas += static_cast<int64_t>(bg[g].S) * cparts;
       Xcur[g] = xa(g);
     }
-    const int gx = static_cast<int>(std::min<int64_t>((max_rc / 8 + 255) / 256 + 1,
-                                                      std::max(1, num_sms() * 8 / ymats)));
-    launch_pdl(to_half_multi_kernel, dim3(gx, ymats), dim3(256), 0, stream, tt, norm_eps, norm_safety);
+    if (ctas > (1ll << 30)) { set_error("orthogonalize: too many elements"); return -1; }
+    launch_pdl(to_half_multi_kernel, dim3(static_cast<unsigned>(ctas)), dim3(256), 0, stream, tt, norm_eps,
+               norm_safety);
     count_launch();
     if (int e = check_launch("to_half_multi")) return e;
   }
