@@ -242,15 +242,19 @@ class ShardedStep:
         self._gather_tables()
 
     @torch.no_grad()
-    def step(self, mark=None):
+    def step(self, mark=None, before=None):
         """One sharded optimizer step: AdamW first, so the all-gathers of the
         vocabulary tables run on NCCL's stream while NorMuon computes; then
         NorMuon, the EMA update and the all-gather of the NorMuon arena.
         Same results as muon.step(); adamw.step(); ema.update(); gather().
         ``mark(name)``, when given, is called after each phase is enqueued
-        (phase timing with events on the current stream)."""
+        (phase timing with events on the current stream); ``before(name)`` is
+        called right before the AdamW ("adamw") and NorMuon ("normuon") steps
+        (a caller streaming gradients in waits there for each optimizer's)."""
         mark = mark or (lambda name: None)
+        before = before or (lambda name: None)
         push_tables = self.exchange in ("ce", "hybrid")
+        before("adamw")
         self.adamw.step()
         mark("adamw")
         works = []
@@ -258,6 +262,7 @@ class ShardedStep:
             self._push("tables")
         elif self.world > 1:
             works = self._gather_tables(async_op=True)
+        before("normuon")
         self.muon.step()
         mark("normuon")
         if self.ema is not None:

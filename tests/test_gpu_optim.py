@@ -351,3 +351,47 @@ def test_gram_small_matrices_match_binary16_emulation(cuda, r, c):
     print(f"({r},{c}) engine vs binary16 emulation {err:.2e}, vs fp64 {err64:.2e}")
     assert err < 1e-2
     assert err64 < 3e-2
+
+
+def test_multi_group_orthogonalisation_equals_per_group(cuda):
+    """Shape groups sharing m = min(r, c) go through one call, whose per-group
+    Gram and Q X products run as grouped GEMM launches (CTA-pair tiles here);
+    grouping changes launch granularity only, so each group's result must be
+    bit-identical to the group orthogonalised alone."""
+    lib = _lib.load()
+    shapes = [(3, 768, 256), (2, 256, 256), (2, 256, 1280), (1, 1024, 256)]
+    opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(4, 4, device=cuda))], orthogonalizer="gram")
+    coeffs, resets, nres = opt._table(5)
+    g = torch.Generator(device=cuda).manual_seed(11)
+    data = []
+    for S, r, c in shapes:
+        U = (torch.randn(S, r, c, generator=g, device=cuda) * 1e-3).to(torch.bfloat16)
+        nparts = lib.b2o_normuon_front_parts(r * c)
+        part = torch.zeros(S, nparts, device=cuda)
+        part[:, 0] = U.float().pow(2).sum(dim=(1, 2))
+        ntn = (c + 255) // 256
+        data.append((U, part, S, r, c, ntn))
+
+    def run(members):
+        groups = (_lib.OrthoGroup * len(members))()
+        outs = []
+        for i, (U, part, S, r, c, ntn) in enumerate(members):
+            o = torch.empty_like(U)
+            rs = torch.zeros(S * ntn * r, device=cuda)
+            outs.append((o, rs))
+            groups[i] = _lib.OrthoGroup(U.data_ptr(), part.data_ptr(), o.data_ptr(), rs.data_ptr(), S, r, c, 0)
+        nbytes = lib.b2o_ortho_workspace_bytes_multi(groups, len(members))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
+        rc = lib.b2o_orthogonalize_multi(groups, len(members), 1, coeffs, 5, resets, nres, opt.norm_eps,
+                                         opt.norm_safety, ws.data_ptr(), nbytes, _lib.stream_ptr())
+        _lib.check(rc, "orthogonalize_multi")
+        torch.cuda.synchronize()
+        return outs
+
+    together = run(data)
+    assert _lib.device_error() == 0
+    for i, d in enumerate(data):
+        (o1, rs1), = run([d])
+        o, rs = together[i]
+        assert torch.equal(o, o1), f"group {d[2:5]}: output differs when grouped"
+        assert torch.equal(rs, rs1), f"group {d[2:5]}: row sums differ when grouped"
