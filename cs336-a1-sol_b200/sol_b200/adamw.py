@@ -73,7 +73,10 @@ class AdamW(torch.optim.Optimizer):
         return super().state_dict()
 
     def load_state_dict(self, state_dict):
-        super().load_state_dict(state_dict)
+        """Keeps each saved state tensor's dtype (fp32 moments of bf16 parameters
+        in master mode; torch's loader would cast them to bf16)."""
+        from .normuon import _load_state_keep_dtypes
+        _load_state_keep_dtypes(self, state_dict)
         for group in self.param_groups:
             for p in group["params"]:
                 st = self.state.get(p)

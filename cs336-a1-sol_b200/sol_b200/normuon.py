@@ -33,6 +33,18 @@ from .polar_express import table_for
 MAX_BATCH = 64  # matrices per launch (kernel-parameter tables)
 
 
+def _load_state_keep_dtypes(opt, state_dict):
+    """torch.optim.Optimizer.load_state_dict without the cast of floating-point
+    state to the parameter dtype: tensors move to the parameter's device only."""
+    saved = state_dict["state"]
+    torch.optim.Optimizer.load_state_dict(opt, {"state": {}, "param_groups": state_dict["param_groups"]})
+    params = [p for g in opt.param_groups for p in g["params"]]
+    for idx, st in saved.items():
+        p = params[int(idx)]
+        opt.state[p] = {k: (v.detach().to(device=p.device).clone() if torch.is_tensor(v) else v)
+                        for k, v in st.items()}
+
+
 class NorMuonGNS(torch.optim.Optimizer):
     """NorMuon (Muon + per-row second moment) with a Newton-Schulz orthogonaliser.
 
@@ -131,6 +143,13 @@ class NorMuonGNS(torch.optim.Optimizer):
                                    ortho.numel(), out.data_ptr(), ws["rowsq"].data_ptr(),
                                    _lib.stream_ptr(U.device))
         _lib.check(rc, "orthogonalize")
+
+    def load_state_dict(self, state_dict):
+        """Loads param groups and per-parameter state keeping each saved tensor's
+        dtype (torch's Optimizer.load_state_dict casts floating-point state to the
+        parameter dtype, which would turn the fp32 v_row of bf16 matrices into
+        bf16)."""
+        _load_state_keep_dtypes(self, state_dict)
 
     def _hook_overridden(self):
         return ("_orthogonalize_batch" in self.__dict__ or

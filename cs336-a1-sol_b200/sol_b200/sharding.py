@@ -283,6 +283,38 @@ class ShardedStep:
         mark("table_wait")
 
     @torch.no_grad()
+    def gather_state(self):
+        """Completes every rank's optimizer state from the owners (for a
+        checkpoint in the reference layout; collectives on every rank): the
+        NorMuon state of each matrix from its owner, the AdamW state of the
+        row-sharded tables from every rank's rows, and the EMA shadows."""
+        if self.world == 1:
+            return
+        for g in self.muon.param_groups:
+            for p in g["params"]:
+                st = self.muon._init_state(p)  # zero state where this rank never stepped p
+                for key in sorted(st):
+                    dist.broadcast(st[key], src=self.owner[id(p)], group=self.group)
+        for p in self.row_sharded:
+            st = self.adamw._init_state(p)
+            for key in ("exp_avg", "exp_avg_sq", "mant_rem"):
+                if key in st:
+                    flat = st[key].view(-1)
+                    per = flat.numel() // self.world
+                    dist.all_gather_into_tensor(flat, flat[self.rank * per:(self.rank + 1) * per].clone(),
+                                                group=self.group)
+        self.gather_ema()
+
+    def drop_unowned_state(self):
+        """Frees the NorMuon state of other ranks' matrices (after a checkpoint)."""
+        if self.world == 1:
+            return
+        for g in self.muon.param_groups:
+            for p in g["params"]:
+                if self.owner[id(p)] != self.rank:
+                    self.muon.state.pop(p, None)
+
+    @torch.no_grad()
     def gather_ema(self):
         """Completes every rank's EMA shadows from their owners (for eval / checkpoints)."""
         if self.ema is None or self.world == 1:
