@@ -29,7 +29,13 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
                   float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
                   float w_beta2, float ema_weight, float* scratch, cudaStream_t stream);
 int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
-                        int nesterov, cudaStream_t stream);
+                        int nesterov, const float* grad_scale, cudaStream_t stream);
+// ---- clip.cu
+int64_t clip_scratch_floats(const int64_t* numels, int n);
+int clip_grad_norm(const void* const* grads, const int64_t* numels, const int* dtypes, int n, float max_norm,
+                   float* scratch, float* out, cudaStream_t stream);
+int clip_scale(void* const* grads, const int64_t* numels, const int* dtypes, int n, const float* coef,
+               cudaStream_t stream);
 int normuon_apply_multi(const b2o_normuon_batch* batches, int nb, int param_dtype, float neg_lr, float lr_wd,
                         float wd_factor, int wd_on, int cautious, float w_beta2, float ema_weight,
                         cudaStream_t stream);

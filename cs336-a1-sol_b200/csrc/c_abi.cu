@@ -182,9 +182,21 @@ int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, i
 }
 
 int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small,
-                            float w_large, int nesterov, void* stream) {
-  return normuon_front_multi(batches, nbatches, dtype, w_small, w_large, nesterov,
+                            float w_large, int nesterov, const float* d_grad_scale, void* stream) {
+  return normuon_front_multi(batches, nbatches, dtype, w_small, w_large, nesterov, d_grad_scale,
                              static_cast<cudaStream_t>(stream));
+}
+
+int64_t b2o_clip_scratch_floats(const int64_t* numels, int n) { return clip_scratch_floats(numels, n); }
+
+int b2o_clip_grad_norm(const void* const* d_grads, const int64_t* numels, const int* dtypes, int n,
+                       float max_norm, float* d_scratch, float* d_out, void* stream) {
+  return clip_grad_norm(d_grads, numels, dtypes, n, max_norm, d_scratch, d_out, static_cast<cudaStream_t>(stream));
+}
+
+int b2o_clip_scale(void* const* d_grads, const int64_t* numels, const int* dtypes, int n, const float* d_coef,
+                   void* stream) {
+  return clip_scale(d_grads, numels, dtypes, n, d_coef, static_cast<cudaStream_t>(stream));
 }
 
 int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int param_dtype, float neg_lr,

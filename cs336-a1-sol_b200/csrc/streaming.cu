@@ -135,11 +135,18 @@ __global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_consta
     uint16_t* __restrict__ R = T.rem;
     float* __restrict__ E = T.ema;
     const float ew = tab.ema_weight;
+    // clipped gradient g = dtype(g * coef), as torch._foreach_mul_ leaves it
+    const float* gsp = tab.g[T.group].grad_scale;
+    const float gs = gsp ? *gsp : 1.0f;
     if (tab.vec_ok[lo]) {
       for (int64_t i = base + static_cast<int64_t>(threadIdx.x) * 8; i + 8 <= end; i += kAdamThreads * 8) {
         float w[8], g[8], m[8], v[8];
         Elem<PT>::load8(P + i, w);
         Elem<PT>::load8(G + i, g);
+        if (gsp) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) g[k] = Elem<PT>::rnd(g[k] * gs);
+        }
         Elem<ST>::load8(M + i, m);
         Elem<ST>::load8(V + i, v);
         if (R) {
@@ -174,6 +181,7 @@ __global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_consta
       const int64_t tail = base + ((end - base) / 8) * 8;
       for (int64_t i = tail + threadIdx.x; i < end; i += kAdamThreads) {
         float w = Elem<PT>::load1(P + i), g = Elem<PT>::load1(G + i);
+        if (gsp) g = Elem<PT>::rnd(g * gs);
         float m = Elem<ST>::load1(M + i), v = Elem<ST>::load1(V + i);
         if (R) w = w + bf16_to_f32(R[i]);
         adam_elem(c, w, g, m, v);
@@ -187,6 +195,7 @@ __global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_consta
     } else {
       for (int64_t i = base + threadIdx.x; i < end; i += kAdamThreads) {
         float w = Elem<PT>::load1(P + i), g = Elem<PT>::load1(G + i);
+        if (gsp) g = Elem<PT>::rnd(g * gs);
         float m = Elem<ST>::load1(M + i), v = Elem<ST>::load1(V + i);
         if (R) w = w + bf16_to_f32(R[i]);
         adam_elem(c, w, g, m, v);
@@ -392,6 +401,7 @@ struct FrontTable {
   MultiHeader h;
   const void* g[kMaxMultiMats];
   void* buf[kMaxMultiMats];
+  const float* gscale;  // gradient-clip coefficient, or null
 };
 
 template <typename T>
@@ -408,6 +418,9 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
   uint16_t* Us = bi.u + static_cast<int64_t>(s) * rc;
   const int64_t base = static_cast<int64_t>(part) * kFrontPart;
   const int64_t end = min(rc, base + kFrontPart);
+  // clipped gradient g = dtype(g * coef), as torch._foreach_mul_ leaves it
+  const bool clip = tab.gscale != nullptr;
+  const float gs = clip ? *tab.gscale : 1.0f;
   float pacc = 0.f;
   int64_t scalar_from = base;
   if (bi.vec_ok) {
@@ -415,6 +428,10 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
       float g[8], b[8], u[8];
       Elem<T>::load8(G + i, g);
       Elem<T>::load8(B + i, b);
+      if (clip) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) g[k] = Elem<T>::rnd(g[k] * gs);
+      }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         b[k] = Elem<T>::rnd(torch_lerp(b[k], g[k], w_small));   // buf.lerp_(g, 1-beta)
@@ -428,7 +445,8 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
     scalar_from = base + ((end - base) / 8) * 8;
   }
   for (int64_t i = scalar_from + threadIdx.x; i < end; i += kFrontThreads) {
-    const float g = Elem<T>::load1(G + i);
+    float g = Elem<T>::load1(G + i);
+    if (clip) g = Elem<T>::rnd(g * gs);
     float b = Elem<T>::load1(B + i);
     b = Elem<T>::rnd(torch_lerp(b, g, w_small));
     float u = nesterov ? Elem<T>::rnd(torch_lerp(g, b, w_large)) : b;
@@ -489,13 +507,14 @@ static int fill_header(const b2o_normuon_batch* batches, int nb, const char* wha
 }
 
 int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
-                        int nesterov, cudaStream_t stream) {
+                        int nesterov, const float* grad_scale, cudaStream_t stream) {
   if (dtype != B2O_F32 && dtype != B2O_BF16) { set_error("normuon_front: bad dtype"); return -1; }
   FrontTable tab;
   int nmats = 0, ncta = 0;
   if (int e = fill_header(batches, nb, "normuon_front", normuon_front_parts, tab.h, nmats, ncta)) return e;
   memset(tab.g, 0, sizeof(tab.g));
   memset(tab.buf, 0, sizeof(tab.buf));
+  tab.gscale = grad_scale;
   for (int k = 0; k < nb; ++k) {
     const b2o_normuon_batch& b = batches[k];
     MultiBatchInfo& bi = tab.h.b[k];
@@ -528,7 +547,7 @@ int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int
   memset(&b, 0, sizeof(b));
   b.S = S; b.r = r; b.c = c;
   b.grads = grads; b.bufs = bufs; b.u = U; b.partial = partial;
-  return normuon_front_multi(&b, 1, dtype, w_small, w_large, nesterov, stream);
+  return normuon_front_multi(&b, 1, dtype, w_small, w_large, nesterov, nullptr, stream);
 }
 
 // ====================================================== NorMuon finish ===

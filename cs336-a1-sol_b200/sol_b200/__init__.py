@@ -6,11 +6,12 @@ Public surface (names of transformer_lm.sol_modules):
   these classes so that train_sol.py runs unchanged.
 """
 from .adamw import AdamW
+from .clip import clip_grad_norm_
 from .ema import EmaWeights
 from .normuon import NorMuonGNS
 from .routing import build_optimizers, route_params
 
-__all__ = ["AdamW", "EmaWeights", "NorMuonGNS", "build_optimizers", "route_params", "install"]
+__all__ = ["AdamW", "EmaWeights", "NorMuonGNS", "build_optimizers", "clip_grad_norm_", "route_params", "install"]
 
 
 def install(module=None):

@@ -48,6 +48,7 @@ class AdamwGroup(C.Structure):
         ("lr_wd", c_float),
         ("step", c_float),
         ("cautious", C.c_int32),
+        ("grad_scale", c_void_p),
     ]
 
 
@@ -128,7 +129,13 @@ SIGNATURES = {
     "b2o_gemm_bf16_simt": (c_int, [c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_int64, c_int,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
                                    c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
-    "b2o_normuon_front_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_int, c_void_p]),
+    "b2o_normuon_front_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_int, c_void_p,
+                                        c_void_p]),
+    "b2o_clip_scratch_floats": (c_int64, [C.POINTER(c_int64), c_int]),
+    "b2o_clip_grad_norm": (c_int, [C.POINTER(c_void_p), C.POINTER(c_int64), C.POINTER(c_int), c_int, c_float,
+                                   c_void_p, c_void_p, c_void_p]),
+    "b2o_clip_scale": (c_int, [C.POINTER(c_void_p), C.POINTER(c_int64), C.POINTER(c_int), c_int, c_void_p,
+                               c_void_p]),
     "b2o_normuon_apply_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_float, c_int,
                                         c_int, c_float, c_float, c_void_p]),
     "b2o_ipc_export": (c_int, [c_void_p, c_void_p, C.POINTER(C.c_uint64)]),

@@ -48,6 +48,7 @@ class AdamW(torch.optim.Optimizer):
         self._owned_slices = None  # id(param) -> (start_elem, numel) this rank updates
         self._ema = None           # EmaWeights folded into the pass (set when it arms)
         self._ema_weight = 0.0
+        self._grad_scale = None    # device fp32 clip coefficient for the next step (clip_grad_norm_ defer_to)
         register_optimizer(self)
 
     def _init_state(self, p):
@@ -116,8 +117,9 @@ class AdamW(torch.optim.Optimizer):
             lr, wd = float(group["lr"]), float(group["weight_decay"])
             # torch's fused kernel multiplies fp32(lr) * fp32(weight_decay)
             lr_wd = float(C.c_float(float(C.c_float(lr).value) * float(C.c_float(wd).value)).value)
+            gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
             gtab.append(_lib.AdamwGroup(lr, float(b1), float(b2), float(group["eps"]), wd, lr_wd,
-                                        float(steps.pop()), int(bool(self.cautious_wd))))
+                                        float(steps.pop()), int(bool(self.cautious_wd)), gs))
         groups = (_lib.AdamwGroup * max(1, len(gtab)))()
         for i, g in enumerate(gtab):
             if g is not None:
@@ -154,4 +156,5 @@ class AdamW(torch.optim.Optimizer):
             rc = lib.b2o_adamw_step(arr, len(descs), groups, len(gtab), _lib.dtype_code(pdt),
                                     _lib.dtype_code(sdt), self._ema_weight, _lib.stream_ptr(dev))
             _lib.check(rc, "adamw_step")
+        self._grad_scale = None
         return loss

@@ -18,7 +18,7 @@ INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libb2o.so"
 BUILD_DIR = PKG_DIR.parent / "_build"
 
-SOURCES = ["c_abi.cu", "streaming.cu", "gemm.cu", "ortho.cu", "peer.cu"]
+SOURCES = ["c_abi.cu", "streaming.cu", "gemm.cu", "ortho.cu", "peer.cu", "clip.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -77,6 +77,7 @@ class NorMuonGNS(torch.optim.Optimizer):
         self._ema = None           # EmaWeights folded into the apply pass (set when it arms)
         self._ema_weight = 0.0
         self._timing_events = None  # list -> (start, end) CUDA events around each orthogonalisation
+        self._grad_scale = None    # device fp32 clip coefficient for the next step (clip_grad_norm_ defer_to)
         register_optimizer(self)
 
     # ------------------------------------------------------------------ hooks
@@ -211,8 +212,9 @@ class NorMuonGNS(torch.optim.Optimizer):
                 arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"], grads=_lib.addr(grads),
                                            bufs=_lib.addr(bufs), u=b["ws"]["u"].data_ptr(),
                                            partial=b["ws"]["partial"].data_ptr())
+            gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
             rc = lib.b2o_normuon_front_multi(arr, len(members), _lib.dtype_code(dt), 1.0 - beta, beta,
-                                             int(bool(group["nesterov"])), _lib.stream_ptr(dev))
+                                             int(bool(group["nesterov"])), gs, _lib.stream_ptr(dev))
             _lib.check(rc, "normuon_front")
 
     def _ortho_class(self, batches, ns_steps):
@@ -317,4 +319,5 @@ class NorMuonGNS(torch.optim.Optimizer):
                        for i in range(0, len(params), MAX_BATCH)]
             if batches:
                 self._step_group(batches, group)
+        self._grad_scale = None
         return loss

@@ -82,6 +82,9 @@ typedef struct {
   float lr_wd;          /* fp32(lr * weight_decay), rounded once on the host  */
   float step;           /* step count after increment (torch's state["step"]) */
   int32_t cautious;     /* 1: decay only where update * w > 0                 */
+  const float* grad_scale;  /* device pointer to a gradient-clip coefficient
+                               (b2o_clip_grad_norm's d_out + 1) applied as
+                               g = dtype(g * coef) before the update, or NULL */
 } b2o_adamw_group;
 
 /* param_dtype: B2O_F32 or B2O_BF16. state_dtype: B2O_F32 or B2O_BF16 (must equal
@@ -190,8 +193,10 @@ typedef struct b2o_normuon_batch {
   float* const* vrows;          /* apply: S fp32 (r, 1) second moments */
   float* scratch;               /* apply: b2o_normuon_apply_scratch_floats(S, r) floats */
 } b2o_normuon_batch;
+/* d_grad_scale: device pointer to a gradient-clip coefficient applied as
+ * g = dtype(g * coef) when the gradients are read, or NULL. */
 int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small,
-                            float w_large, int nesterov, void* stream);
+                            float w_large, int nesterov, const float* d_grad_scale, void* stream);
 int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int param_dtype, float neg_lr,
                             float lr_wd, float wd_factor, int wd_on, int cautious, float w_beta2,
                             float ema_weight, void* stream);
@@ -263,6 +268,23 @@ int b2o_gemm_bf16_simt(const uint16_t* d_A, int64_t lda, int64_t strideA, int a_
                        int M, int N, int K, int batch, int epi,
                        float alpha, float beta, float gamma, const float* d_scale,
                        float* d_rowsq, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Gradient-norm clip: torch.nn.utils.clip_grad_norm_(params, max_norm,
+ * foreach=True) as the reference calls it before the optimizer steps
+ * (transformer_lm/train_sol.py:498-499), with torch's dtype semantics: each
+ * tensor's norm rounded to its gradient dtype, the total and the coefficient
+ * min(max_norm / (total + 1e-6), 1) rounded to the promoted dtype.
+ * b2o_clip_scratch_floats: scratch floats a call needs (one per 32768 elements).
+ * b2o_clip_grad_norm: d_out[0] = total norm, d_out[1] = clip coefficient.
+ * b2o_clip_scale: g = dtype(g * d_coef[0]) in place (torch._foreach_mul_);
+ *   or hand d_out + 1 to the optimizers' grad_scale arguments instead.
+ * dtypes: B2O_F32 or B2O_BF16 per tensor; at most 1024 tensors per call. */
+int64_t b2o_clip_scratch_floats(const int64_t* numels, int n);
+int b2o_clip_grad_norm(const void* const* d_grads, const int64_t* numels, const int* dtypes, int n,
+                       float max_norm, float* d_scratch, float* d_out, void* stream);
+int b2o_clip_scale(void* const* d_grads, const int64_t* numels, const int* dtypes, int n, const float* d_coef,
+                   void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Peer exchange for the sharded step on the GPUs of one node (no reference

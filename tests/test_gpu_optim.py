@@ -395,3 +395,48 @@ def test_multi_group_orthogonalisation_equals_per_group(cuda):
         o, rs = together[i]
         assert torch.equal(o, o1), f"group {d[2:5]}: output differs when grouped"
         assert torch.equal(rs, rs1), f"group {d[2:5]}: row sums differ when grouped"
+
+
+# -------------------------------------------------------- gradient clip --
+@pytest.mark.parametrize("max_norm", [1e-3, 1e3])
+def test_clip_grad_norm_matches_torch(cuda, max_norm):
+    """sol_b200.clip_grad_norm_ vs torch.nn.utils.clip_grad_norm_(foreach=True)
+    (train_sol.py:498-499) on the recipe's bf16 gradients, clipping (1e-3) and
+    not (1e3): the returned norm and the clipped gradients are bit-identical."""
+    from sol_b200 import clip_grad_norm_
+    model = synth.SyntheticLM(synth.MICRO, device=cuda, seed=0)
+    grads = synth.make_grads(model, 0, seed=0)
+    params = [p for _, p in model.named_parameters()]
+    for p, g in zip(params, grads):
+        p.grad = g.clone()
+    ref = torch.nn.utils.clip_grad_norm_(params, max_norm, foreach=True)
+    ref_grads = [p.grad.clone() for p in params]
+    for p, g in zip(params, grads):
+        p.grad = g.clone()
+    got = clip_grad_norm_(params, max_norm, foreach=True)
+    torch.cuda.synchronize()
+    assert got.dtype == ref.dtype and float(got) == float(ref), (float(got), float(ref))
+    for p, r in zip(params, ref_grads):
+        assert torch.equal(p.grad, r)
+
+
+def test_deferred_clip_step_equals_eager_clip_step(cuda):
+    """Clipping deferred into the optimizers' passes gives the same step as
+    clipping the gradients in place first."""
+    from sol_b200 import clip_grad_norm_
+
+    def run(defer):
+        model = synth.SyntheticLM(synth.MICRO, device=cuda, seed=0)
+        muon, adamw = build_optimizers(model, adam_master="bf16_mt", muon_lr=8e-3, adam_lr=1.2e-2,
+                                       embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+        params = [p for _, p in model.named_parameters()]
+        for k in range(3):
+            synth.set_grads(model, synth.make_grads(model, k, seed=0))
+            clip_grad_norm_(params, 2e-3, defer_to=(muon, adamw) if defer else None)
+            muon.step()
+            adamw.step()
+        torch.cuda.synchronize()
+        return [p.detach().clone() for p in params]
+
+    for a, b in zip(run(False), run(True)):
+        assert torch.equal(a, b)

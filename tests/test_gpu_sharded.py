@@ -64,7 +64,19 @@ def _worker(rank, world, port, exchange, q):
         sharded.gather_ema()
         torch.cuda.synchronize()
         bad_ema = [n for (n, _), s, r in zip(named, ema.shadow, rema.shadow) if not torch.equal(s, r)]
-        q.put((rank, {"exchange": sharded.exchange, "bad": bad, "bad_ema": bad_ema, "owned": len(muon._owned)}))
+        # checkpoint path: every rank's optimizer state completed from the owners
+        sharded.gather_state()
+        torch.cuda.synchronize()
+        bad_state = []
+        for a, b in ((muon, rmuon), (adamw, radamw)):
+            pa = [p for g in a.param_groups for p in g["params"]]
+            pb = [p for g in b.param_groups for p in g["params"]]
+            for i, (p, r) in enumerate(zip(pa, pb)):
+                for k, v in b.state[r].items():
+                    if k != "step" and not torch.equal(a.state[p][k], v):
+                        bad_state.append((type(a).__name__, i, k))
+        q.put((rank, {"exchange": sharded.exchange, "bad": bad, "bad_ema": bad_ema, "bad_state": bad_state,
+                      "owned": len(muon._owned)}))
     except Exception as e:  # noqa: BLE001
         q.put((rank, f"error: {type(e).__name__}: {e}"))
     finally:
@@ -104,4 +116,5 @@ def test_sharded_step_bit_identical_to_single_gpu(exchange):
         assert v["exchange"] == exchange
         assert v["bad"] == [], (r, v["bad"])
         assert v["bad_ema"] == [], (r, v["bad_ema"])
+        assert v["bad_state"] == [], (r, v["bad_state"])
     assert sum(v["owned"] for v in out.values()) == 3 * 5  # MICRO: 3 layers x 5 NorMuon matrices
