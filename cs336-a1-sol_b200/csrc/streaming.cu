@@ -126,6 +126,9 @@ __global__ void __launch_bounds__(kAdamThreads) adamw_kernel(const __grid_consta
     }
     const b2o_adamw_tensor& T = tab.t[lo];
     const AdamCoef c = make_coef(tab.g[T.group]);
+    // torch's fused AdamW keeps state["step"] on the device: the CTA of the
+    // tensor's first chunk writes it
+    if (T.step_out && chunk == tab.chunk_start[lo] && threadIdx.x == 0) *T.step_out = tab.g[T.group].step;
     const int64_t base = static_cast<int64_t>(chunk - tab.chunk_start[lo]) * kAdamChunk;
     const int64_t end = min(T.numel, base + kAdamChunk);
     PT* __restrict__ P = reinterpret_cast<PT*>(T.param);

@@ -35,6 +35,7 @@ class AdamwTensor(C.Structure):
         ("numel", c_int64),
         ("group", C.c_int32),
         ("_pad", C.c_int32),
+        ("step_out", c_void_p),
     ]
 
 

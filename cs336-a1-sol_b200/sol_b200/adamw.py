@@ -65,13 +65,6 @@ class AdamW(torch.optim.Optimizer):
             self._steps[id(p)] = int(st["step"].item()) if st["step"].device.type == "cpu" else 0
         return st
 
-    def state_dict(self):
-        for group in self.param_groups:
-            for p in group["params"]:
-                st = self.state.get(p)
-                if st and "step" in st:
-                    st["step"].fill_(float(self._steps.get(id(p), 0)))
-        return super().state_dict()
 
     def load_state_dict(self, state_dict):
         """Keeps each saved state tensor's dtype (fp32 moments of bf16 parameters
@@ -144,7 +137,7 @@ class AdamW(torch.optim.Optimizer):
                     st["exp_avg"].data_ptr() + start * ssz,
                     st["exp_avg_sq"].data_ptr() + start * ssz,
                     (shadow.data_ptr() + start * 4) if shadow is not None else None,
-                    n, gi, 0))
+                    n, gi, 0, st["step"].data_ptr()))
             if not descs:
                 continue
             if self._ema is not None:

@@ -71,6 +71,8 @@ typedef struct {
   int64_t numel;
   int32_t group;        /* index into the group table                         */
   int32_t _pad;
+  float* step_out;      /* 0-d fp32 step tensor (torch's state["step"]) that the
+                           pass sets to the group's step, or NULL             */
 } b2o_adamw_tensor;
 
 typedef struct {

@@ -48,6 +48,7 @@ def _fill_state(model, muon, adamw, owned=None, rows=None):
                     st[k].view(-1)[start:start + cnt].copy_(full.view(-1)[start:start + cnt])
                 else:
                     st[k].copy_(full)
+            st["step"].fill_(7.0)
             adamw._steps[id(p)] = 7
 
 
