@@ -30,6 +30,8 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
                   float w_beta2, float ema_weight, float* scratch, cudaStream_t stream);
 int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
                         int nesterov, const float* grad_scale, cudaStream_t stream);
+int normuon_prescale(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                     int nesterov, const float* grad_scale, float norm_eps, float norm_safety, cudaStream_t stream);
 // ---- clip.cu
 int64_t clip_scratch_floats(const int64_t* numels, int n);
 int clip_grad_norm(const void* const* grads, const int64_t* numels, const int* dtypes, int n, float max_norm,
@@ -85,11 +87,12 @@ struct GemmTimer {
 
 // ---- ortho.cu
 struct OrthoGroup {
-  const uint16_t* U;       // front output (S, r, c) bf16
+  const uint16_t* U;       // front output (S, r, c): bf16 u, or binary16 X0 when xscale is set
   const float* partial;    // front sum-of-squares partials
   uint16_t* out;           // o (S, r, c) bf16
   float* rowsq;            // per-row partial sums of o^2
   int S, r, c;
+  const float* xscale;     // Gram mode, prescaled X0: [S] s_norm / k, [S, 2S) squares; else null
 };
 int64_t ortho_workspace_bytes(int S, int r, int c);
 int64_t ortho_workspace_bytes_multi(const OrthoGroup* g, int ng);

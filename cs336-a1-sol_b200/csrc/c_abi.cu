@@ -149,7 +149,8 @@ int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r,
 
 static std::vector<OrthoGroup> to_groups(const b2o_ortho_group* g, int ng) {
   std::vector<OrthoGroup> v;
-  for (int i = 0; i < ng; ++i) v.push_back(OrthoGroup{g[i].u, g[i].partial, g[i].out, g[i].rowsq, g[i].S, g[i].r, g[i].c});
+  for (int i = 0; i < ng; ++i)
+    v.push_back(OrthoGroup{g[i].u, g[i].partial, g[i].out, g[i].rowsq, g[i].S, g[i].r, g[i].c, g[i].xscale});
   return v;
 }
 
@@ -185,6 +186,12 @@ int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int 
                             float w_large, int nesterov, const float* d_grad_scale, void* stream) {
   return normuon_front_multi(batches, nbatches, dtype, w_small, w_large, nesterov, d_grad_scale,
                              static_cast<cudaStream_t>(stream));
+}
+
+int b2o_normuon_prescale(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small, float w_large,
+                         int nesterov, const float* d_grad_scale, float norm_eps, float norm_safety, void* stream) {
+  return normuon_prescale(batches, nbatches, dtype, w_small, w_large, nesterov, d_grad_scale, norm_eps, norm_safety,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int64_t b2o_clip_scratch_floats(const int64_t* numels, int n) { return clip_scratch_floats(numels, n); }

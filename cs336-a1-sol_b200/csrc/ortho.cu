@@ -436,6 +436,9 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     }
   }
   if (mode != 0 && mode != 1) { set_error("orthogonalize: mode must be 0 or 1"); return -1; }
+  for (int i = 0; i < ng; ++i) {
+    if (groups[i].xscale && mode != 1) { set_error("orthogonalize: prescaled input is for Gram mode"); return -1; }
+  }
   if (T < 1 || T > 64) { set_error("orthogonalize: 1..64 steps"); return -1; }
   if (nresets < 0 || (nresets > 0 && !resets)) { set_error("orthogonalize: bad resets"); return -1; }
   OrthoLayout L;
@@ -464,6 +467,9 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   // small matrices: one kernel per group does the whole iteration
   bool small = mode == 1 && L.m <= kSmallM;
   for (int g = 0; g < ng; ++g) small = small && static_cast<int64_t>(bg[g].m) * bg[g].n <= kSmallElems;
+  for (int g = 0; g < ng && small; ++g) {
+    if (groups[g].xscale) { set_error("orthogonalize: small matrices take the bf16 front output"); return -1; }
+  }
   if (small) {
     SmallNsArgs sa;
     memset(&sa, 0, sizeof(sa));
@@ -544,14 +550,26 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   // normalised binary16 copy of each front output (the Gram iteration runs in
   // binary16: R, P and Q are bounded, and its 11-bit significand keeps the
   // Gram matrix far more accurate than bfloat16 at the same tensor-core rate)
+  // Xcur: the iterate each group's products read; xs: its per-matrix factor
+  // while it is a prescaled X0 (binary16(u * k), factor s_norm / k), else null
   std::vector<const uint16_t*> Xcur(ng);
-  for (int g0 = 0; g0 < ng; g0 += kToHalfGroups) {
+  std::vector<const float*> xs(ng, nullptr);
+  std::vector<int> conv;
+  for (int g = 0; g < ng; ++g) {
+    if (groups[g].xscale) {
+      Xcur[g] = groups[g].U;
+      xs[g] = groups[g].xscale;
+    } else {
+      conv.push_back(g);
+    }
+  }
+  for (size_t c0 = 0; c0 < conv.size(); c0 += kToHalfGroups) {
     ToHalfTable tt;
     memset(&tt, 0, sizeof(tt));
-    tt.ng = std::min(kToHalfGroups, ng - g0);
+    tt.ng = static_cast<int>(std::min<size_t>(kToHalfGroups, conv.size() - c0));
     int64_t ctas = 0;
     for (int i = 0; i < tt.ng; ++i) {
-      const int g = g0 + i;
+      const int g = conv[c0 + i];
       const int cparts = static_cast<int>((bg[g].rc + kToHalfPart - 1) / kToHalfPart);
       tt.g[i] = ToHalfGroup{groups[g].U, xa(g), groups[g].partial, bg[g].rc, normuon_front_parts(bg[g].rc),
                             cparts, static_cast<int>(ctas)};
@@ -565,8 +583,8 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     if (int e = check_launch("to_half_multi")) return e;
   }
   int R = alloc();
-  for (int g = 0; g < ng; ++g)
-    if ((rc_ = syrk(bg[g], Xcur[g], pool_g(R, g), nullptr))) return rc_;
+  for (int g = 0; g < ng; ++g)  // R = (s_norm / k)^2 X0 X0^T for a prescaled X0
+    if ((rc_ = syrk(bg[g], Xcur[g], pool_g(R, g), xs[g] ? xs[g] + bg[g].S : nullptr))) return rc_;
   int Q = -1;
   for (int t = 0; t < T; ++t) {
     const float a = coeffs[3 * t], bb = coeffs[3 * t + 1], cc = coeffs[3 * t + 2];
@@ -574,9 +592,10 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
       const int Rn = alloc();
       for (int g = 0; g < ng; ++g) {
         uint16_t* Xn = (Xcur[g] == xa(g)) ? xb(g) : xa(g);
-        if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], epi0(Xn, 0, 0, 1.0f, nullptr, 1)))) return rc_;
+        if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], epi0(Xn, 0, 0, 1.0f, xs[g], 1)))) return rc_;
         if ((rc_ = syrk(bg[g], Xn, pool_g(Rn, g), nullptr))) return rc_;
         Xcur[g] = Xn;
+        xs[g] = nullptr;
       }
       release(Q); Q = -1;
       release(R); R = Rn;
@@ -609,7 +628,7 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     if (R < 0 || Q < 0) { set_error("orthogonalize: workspace pool exhausted"); return -1; }
   }
   for (int g = 0; g < ng; ++g) {
-    Epilogue ef = epi0(groups[g].out, 0, 0, 1.0f, nullptr, 0);  // o in bfloat16, as the reference returns it
+    Epilogue ef = epi0(groups[g].out, 0, 0, 1.0f, xs[g], 0);  // o in bfloat16, as the reference returns it
     ef.rowsq = groups[g].rowsq;
     if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], ef))) return rc_;
   }

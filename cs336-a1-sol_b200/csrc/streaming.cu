@@ -387,6 +387,10 @@ struct MultiBatchInfo {
   uint16_t* u;           // front output / apply input o
   float* partial;        // front: norm partials; apply: scratch (S * (r + 4))
   const float* rowsq;    // apply: [S][ceil(c/256)][r]
+  int x0_half;           // front: write binary16 X0 = bf16(u) * prescale[s] instead of bf16 u
+  float* prescale;       // [S] powers of two (0 = none yet)
+  float* xscale;         // [2S] s_norm / k and its square
+  int* flags;            // [S] 1 = X0 needs rewriting with the new k
 };
 struct MultiHeader {
   int nb;
@@ -407,18 +411,34 @@ struct FrontTable {
   const float* gscale;  // gradient-clip coefficient, or null
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __grid_constant__ FrontTable tab,
-                                                                      float w_small, float w_large, int nesterov) {
-  pdl_wait();
+// Stores 8 values of u as bf16, or as binary16 X0 = bf16(u) * k (exact: k is a power of two).
+__device__ __forceinline__ void store_u8(uint16_t* dst, const float* u, bool x0, float k) {
+  if (x0) {
+    U16x8 a;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a.v[i] = f32_to_f16(u[i] * k);
+    *reinterpret_cast<U16x8*>(dst) = a;
+  } else {
+    Elem<uint16_t>::store8(dst, u);
+  }
+}
+
+// REPAIR = false: the front pass (momentum update, u, norm partials).
+// REPAIR = true: rewrites X0 of the matrices flagged by the prescale pass from
+// the gradient and the already updated momentum buffer (no state changes).
+template <typename T, bool REPAIR>
+__device__ __forceinline__ void front_body(const FrontTable& tab, float w_small, float w_large, int nesterov) {
   const MultiBatchInfo& bi = tab.h.b[find_batch_cta(tab.h, blockIdx.x)];
   const int local = blockIdx.x - bi.cta0;
   const int s = local / bi.nparts;
   const int part = local - s * bi.nparts;
+  if (REPAIR && (!bi.x0_half || !bi.flags[s])) return;
   const int64_t rc = bi.rc;
   const T* G = reinterpret_cast<const T*>(tab.g[bi.mat0 + s]);
   T* B = reinterpret_cast<T*>(tab.buf[bi.mat0 + s]);
   uint16_t* Us = bi.u + static_cast<int64_t>(s) * rc;
+  const bool x0 = bi.x0_half != 0;
+  const float k = x0 ? bi.prescale[s] : 1.0f;
   const int64_t base = static_cast<int64_t>(part) * kFrontPart;
   const int64_t end = min(rc, base + kFrontPart);
   // clipped gradient g = dtype(g * coef), as torch._foreach_mul_ leaves it
@@ -433,17 +453,17 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
       Elem<T>::load8(B + i, b);
       if (clip) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) g[k] = Elem<T>::rnd(g[k] * gs);
+        for (int q = 0; q < 8; ++q) g[q] = Elem<T>::rnd(g[q] * gs);
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        b[k] = Elem<T>::rnd(torch_lerp(b[k], g[k], w_small));   // buf.lerp_(g, 1-beta)
-        u[k] = nesterov ? Elem<T>::rnd(torch_lerp(g[k], b[k], w_large)) : b[k];  // g.lerp(buf, beta)
-        u[k] = round_bf16(u[k]);                                 // X = u.bfloat16()
-        pacc = fmaf(u[k], u[k], pacc);
+      for (int q = 0; q < 8; ++q) {
+        if (!REPAIR) b[q] = Elem<T>::rnd(torch_lerp(b[q], g[q], w_small));  // buf.lerp_(g, 1-beta)
+        u[q] = nesterov ? Elem<T>::rnd(torch_lerp(g[q], b[q], w_large)) : b[q];  // g.lerp(buf, beta)
+        u[q] = round_bf16(u[q]);                                                  // X = u.bfloat16()
+        pacc = fmaf(u[q], u[q], pacc);
       }
-      Elem<T>::store8(B + i, b);
-      Elem<uint16_t>::store8(Us + i, u);
+      if (!REPAIR) Elem<T>::store8(B + i, b);
+      store_u8(Us + i, u, x0, k);
     }
     scalar_from = base + ((end - base) / 8) * 8;
   }
@@ -451,13 +471,14 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
     float g = Elem<T>::load1(G + i);
     if (clip) g = Elem<T>::rnd(g * gs);
     float b = Elem<T>::load1(B + i);
-    b = Elem<T>::rnd(torch_lerp(b, g, w_small));
+    if (!REPAIR) b = Elem<T>::rnd(torch_lerp(b, g, w_small));
     float u = nesterov ? Elem<T>::rnd(torch_lerp(g, b, w_large)) : b;
     u = round_bf16(u);
     pacc = fmaf(u, u, pacc);
-    Elem<T>::store1(B + i, b);
-    Us[i] = f32_to_bf16(u);
+    if (!REPAIR) Elem<T>::store1(B + i, b);
+    Us[i] = x0 ? f32_to_f16(u * k) : f32_to_bf16(u);
   }
+  if (REPAIR) return;
   // deterministic block reduction of this part
   __shared__ float red[kFrontThreads / 32];
 #pragma unroll
@@ -466,9 +487,56 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __gr
   __syncthreads();
   if (threadIdx.x == 0) {
     float t = 0.f;
-    for (int k = 0; k < kFrontThreads / 32; ++k) t += red[k];
+    for (int q = 0; q < kFrontThreads / 32; ++q) t += red[q];
     bi.partial[static_cast<int64_t>(s) * bi.nparts + part] = t;
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __grid_constant__ FrontTable tab,
+                                                                      float w_small, float w_large, int nesterov) {
+  pdl_wait();
+  front_body<T, false>(tab, w_small, w_large, nesterov);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFrontThreads) normuon_x0_repair_kernel(const __grid_constant__ FrontTable tab,
+                                                                          float w_small, float w_large,
+                                                                          int nesterov) {
+  pdl_wait();
+  front_body<T, true>(tab, w_small, w_large, nesterov);
+}
+
+// One thread per matrix of the x0_half batches: this step's norm scale, the
+// factor s_norm / k for the orthogonaliser and next step's k = 2^(8 + e) with
+// s_norm in [2^(e-1), 2^e): ||X0|| ~ 2^8 keeps X0's entries far from both ends
+// of binary16. A matrix whose ||X0|| = k / s_norm left [2^2, 2^14] (or that had
+// no k yet) is flagged and rewritten with the new k.
+__global__ void __launch_bounds__(128) normuon_prescale_kernel(const __grid_constant__ MultiHeader h, int nmats,
+                                                               float eps, float safety) {
+  pdl_wait();
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= nmats) return;
+  int kb = 0;
+  while (kb + 1 < h.nb && m >= h.b[kb + 1].mat0) ++kb;
+  const MultiBatchInfo& bi = h.b[kb];
+  if (!bi.x0_half) return;
+  const int s = m - bi.mat0;
+  float acc = 0.f;
+  for (int i = 0; i < bi.nparts; ++i) acc += bi.partial[static_cast<int64_t>(s) * bi.nparts + i];
+  const float sn = 1.0f / (sqrtf(acc) * safety + eps);
+  int e = 0;
+  frexpf(sn, &e);
+  const float k_new = ldexpf(1.0f, e + 8);
+  const float k_old = bi.prescale[s];
+  const float x0norm = k_old / sn;  // ||X0|| written with k_old
+  const bool ok = k_old > 0.f && x0norm >= 4.0f && x0norm <= 16384.0f;
+  const float k = ok ? k_old : k_new;
+  bi.flags[s] = ok ? 0 : 1;
+  bi.prescale[s] = k_new;
+  const float f = sn / k;
+  bi.xscale[s] = f;
+  bi.xscale[bi.S + s] = f * f;
 }
 
 // Checks the batch list shared by the multi-batch calls and fills the header
@@ -509,8 +577,11 @@ static int fill_header(const b2o_normuon_batch* batches, int nb, const char* wha
   return 0;
 }
 
-int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
-                        int nesterov, const float* grad_scale, cudaStream_t stream) {
+// repair = false: the front pass; true: the prescale pass that follows it
+// (same batches and arguments).
+static int front_launch(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                        int nesterov, const float* grad_scale, bool repair, float norm_eps, float norm_safety,
+                        cudaStream_t stream) {
   if (dtype != B2O_F32 && dtype != B2O_BF16) { set_error("normuon_front: bad dtype"); return -1; }
   FrontTable tab;
   int nmats = 0, ncta = 0;
@@ -532,6 +603,28 @@ int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, flo
     bi.vec_ok = vec_ok;
     bi.u = b.u;
     bi.partial = b.partial;
+    bi.x0_half = b.x0_half;
+    bi.prescale = b.prescale;
+    bi.xscale = b.xscale;
+    bi.flags = b.flags;
+    if (b.x0_half && (!b.prescale || !b.xscale || !b.flags)) {
+      set_error("normuon_front: x0_half needs prescale, xscale and flags"); return -1;
+    }
+  }
+  if (repair) {
+    // this step's scales, next step's k, flags; then X0 of the flagged matrices
+    launch_pdl(normuon_prescale_kernel, dim3((nmats + 127) / 128), dim3(128), 0, stream, tab.h, nmats, norm_eps,
+               norm_safety);
+    count_launch();
+    if (int e = check_launch("normuon_prescale")) return e;
+    if (dtype == B2O_F32)
+      launch_pdl(normuon_x0_repair_kernel<float>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small,
+                 w_large, nesterov);
+    else
+      launch_pdl(normuon_x0_repair_kernel<uint16_t>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small,
+                 w_large, nesterov);
+    count_launch();
+    return check_launch("normuon_x0_repair");
   }
   if (dtype == B2O_F32)
     launch_pdl(normuon_front_kernel<float>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small, w_large,
@@ -541,6 +634,17 @@ int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, flo
                w_large, nesterov);
   count_launch();
   return check_launch("normuon_front");
+}
+
+int normuon_front_multi(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                        int nesterov, const float* grad_scale, cudaStream_t stream) {
+  return front_launch(batches, nb, dtype, w_small, w_large, nesterov, grad_scale, false, 0.f, 1.f, stream);
+}
+
+int normuon_prescale(const b2o_normuon_batch* batches, int nb, int dtype, float w_small, float w_large,
+                     int nesterov, const float* grad_scale, float norm_eps, float norm_safety, cudaStream_t stream) {
+  return front_launch(batches, nb, dtype, w_small, w_large, nesterov, grad_scale, true, norm_eps, norm_safety,
+                      stream);
 }
 
 int normuon_front(const void* const* grads, void* const* bufs, int S, int r, int c, int dtype,

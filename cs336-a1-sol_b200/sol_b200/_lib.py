@@ -71,6 +71,11 @@ class NormuonBatch(C.Structure):
         ("emas", c_void_p),
         ("vrows", c_void_p),
         ("scratch", c_void_p),
+        ("prescale", c_void_p),
+        ("xscale", c_void_p),
+        ("flags", c_void_p),
+        ("x0_half", C.c_int32),
+        ("_pad", C.c_int32),
     ]
 
 
@@ -84,6 +89,7 @@ class OrthoGroup(C.Structure):
         ("r", C.c_int32),
         ("c", C.c_int32),
         ("_pad", C.c_int32),
+        ("xscale", c_void_p),
     ]
 
 
@@ -132,6 +138,8 @@ SIGNATURES = {
                                    c_int, c_int, c_float, c_float, c_float, c_void_p, c_void_p, c_void_p]),
     "b2o_normuon_front_multi": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_int, c_void_p,
                                         c_void_p]),
+    "b2o_normuon_prescale": (c_int, [C.POINTER(NormuonBatch), c_int, c_int, c_float, c_float, c_int, c_void_p,
+                                     c_float, c_float, c_void_p]),
     "b2o_clip_scratch_floats": (c_int64, [C.POINTER(c_int64), c_int]),
     "b2o_clip_grad_norm": (c_int, [C.POINTER(c_void_p), C.POINTER(c_int64), C.POINTER(c_int), c_int, c_float,
                                    c_void_p, c_void_p, c_void_p]),

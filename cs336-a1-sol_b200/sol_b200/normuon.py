@@ -122,6 +122,11 @@ class NorMuonGNS(torch.optim.Optimizer):
                 "scratch": torch.empty(lib.b2o_normuon_apply_scratch_floats(S, r), dtype=torch.float32,
                                        device=device),
                 "ortho_bytes": wbytes,
+                # binary16 X0 written by the front: per-matrix power-of-two scale
+                # (kept across steps), this step's factors, repair flags
+                "prescale": torch.zeros(S, dtype=torch.float32, device=device),
+                "xscale": torch.zeros(2 * S, dtype=torch.float32, device=device),
+                "flags": torch.zeros(S, dtype=torch.int32, device=device),
             }
             self._ws[key] = ws
         return ws
@@ -179,7 +184,12 @@ class NorMuonGNS(torch.optim.Optimizer):
                 raise ValueError("NorMuonGNS needs contiguous params and grads of the param dtype")
         states = [self._init_state(p) for p in params]
         ws = self._workspace(dev, S, r, c)
-        return dict(params=params, states=states, ws=ws, S=S, r=r, c=c, dev=dev, o=ws["o"])
+        m, n = min(r, c), max(r, c)
+        # the front writes the Gram iteration's binary16 input directly unless
+        # the batch takes the one-CTA small-matrix path or another orthogonaliser
+        x0 = (self.orthogonalizer == "gram" and not self._hook_overridden() and
+              not (m <= 32 and m * n <= 49152))
+        return dict(params=params, states=states, ws=ws, S=S, r=r, c=c, dev=dev, o=ws["o"], x0=x0)
 
     @staticmethod
     def _calls(recs, key):
@@ -209,13 +219,18 @@ class NorMuonGNS(torch.optim.Optimizer):
                 grads = _lib.ptr_array([p.grad.data_ptr() for p in b["params"]])
                 bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in b["states"]])
                 keep += [grads, bufs]
+                ws = b["ws"]
                 arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"], grads=_lib.addr(grads),
-                                           bufs=_lib.addr(bufs), u=b["ws"]["u"].data_ptr(),
-                                           partial=b["ws"]["partial"].data_ptr())
+                                           bufs=_lib.addr(bufs), u=ws["u"].data_ptr(),
+                                           partial=ws["partial"].data_ptr(), prescale=ws["prescale"].data_ptr(),
+                                           xscale=ws["xscale"].data_ptr(), flags=ws["flags"].data_ptr(),
+                                           x0_half=int(b["x0"]))
             gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
-            rc = lib.b2o_normuon_front_multi(arr, len(members), _lib.dtype_code(dt), 1.0 - beta, beta,
-                                             int(bool(group["nesterov"])), gs, _lib.stream_ptr(dev))
-            _lib.check(rc, "normuon_front")
+            args = (arr, len(members), _lib.dtype_code(dt), 1.0 - beta, beta, int(bool(group["nesterov"])), gs)
+            _lib.check(lib.b2o_normuon_front_multi(*args, _lib.stream_ptr(dev)), "normuon_front")
+            if any(b["x0"] for b in members):
+                _lib.check(lib.b2o_normuon_prescale(*args, self.norm_eps, self.norm_safety, _lib.stream_ptr(dev)),
+                           "normuon_prescale")
 
     def _ortho_class(self, batches, ns_steps):
         """Orthogonalises every batch of one m = min(r, c) class with one library call."""
@@ -227,7 +242,8 @@ class NorMuonGNS(torch.optim.Optimizer):
         for i, b in enumerate(batches):
             ws = b["ws"]
             groups[i] = _lib.OrthoGroup(ws["u"].data_ptr(), ws["partial"].data_ptr(), ws["o"].data_ptr(),
-                                        ws["rowsq"].data_ptr(), b["S"], b["r"], b["c"], 0)
+                                        ws["rowsq"].data_ptr(), b["S"], b["r"], b["c"], 0,
+                                        ws["xscale"].data_ptr() if b.get("x0") else None)
         key = ("multi",) + tuple((b["S"], b["r"], b["c"]) for b in batches)
         nbytes = lib.b2o_ortho_workspace_bytes_multi(groups, len(batches))
         ortho = self._ortho_ws(dev, key, nbytes)

@@ -145,11 +145,14 @@ int b2o_orthogonalize(const uint16_t* d_u, const float* d_partial, int S, int r,
  * its orthogonaliser once per exact shape, sol_modules.py:380-395; grouping by
  * m only changes launch granularity, not any matrix's arithmetic). */
 typedef struct {
-  const uint16_t* u;      /* front output (S, r, c) bf16            */
+  const uint16_t* u;      /* front output (S, r, c): bf16 u, or binary16 X0 (xscale != NULL) */
   const float* partial;   /* front sum-of-squares partials          */
   uint16_t* out;          /* o (S, r, c) bf16                        */
   float* rowsq;           /* S * r * ceil(c/256) floats              */
   int32_t S, r, c, _pad;
+  const float* xscale;    /* Gram mode: u holds X0 = binary16(u * k) with a per-matrix power of two k
+                             (b2o_normuon_prescale); xscale[s] = s_norm / k, xscale[S + s] = its square;
+                             NULL: u is the bf16 front output */
 } b2o_ortho_group;
 int64_t b2o_ortho_workspace_bytes_multi(const b2o_ortho_group* groups, int ngroups);
 int b2o_orthogonalize_multi(const b2o_ortho_group* groups, int ngroups, int mode,
@@ -194,11 +197,26 @@ typedef struct b2o_normuon_batch {
   float* const* emas;           /* apply: S fp32 EMA shadows, or NULL */
   float* const* vrows;          /* apply: S fp32 (r, 1) second moments */
   float* scratch;               /* apply: b2o_normuon_apply_scratch_floats(S, r) floats */
+  float* prescale;              /* front, x0_half: S per-matrix powers of two k (kept across steps; 0 = none) */
+  float* xscale;                /* b2o_normuon_prescale output: 2 * S factors for b2o_ortho_group.xscale */
+  int32_t* flags;               /* b2o_normuon_prescale scratch: S ints */
+  int32_t x0_half;              /* front: write X0 = binary16(bf16(u) * k) instead of bf16 u */
+  int32_t _pad;
 } b2o_normuon_batch;
 /* d_grad_scale: device pointer to a gradient-clip coefficient applied as
  * g = dtype(g * coef) when the gradients are read, or NULL. */
 int b2o_normuon_front_multi(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small,
                             float w_large, int nesterov, const float* d_grad_scale, void* stream);
+/* Gram-mode input without a conversion pass: a front call with x0_half writes
+ * X0 = binary16(bf16(u) * k), k = prescale[s] (a power of two near 256 / ||u||
+ * of the previous step, so the conversion is exact); this call then computes
+ * this step's s_norm = 1 / (||u|| * safety + eps) from the partials, the
+ * factors s_norm / k for the orthogonaliser, and next step's k, and rewrites
+ * X0 of every matrix whose norm left k's range (factor 64 either way; every
+ * matrix on the first step) from its gradient and momentum buffer. Arguments
+ * as for the front call that preceded it. */
+int b2o_normuon_prescale(const b2o_normuon_batch* batches, int nbatches, int dtype, float w_small, float w_large,
+                         int nesterov, const float* d_grad_scale, float norm_eps, float norm_safety, void* stream);
 int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int param_dtype, float neg_lr,
                             float lr_wd, float wd_factor, int wd_on, int cautious, float w_beta2,
                             float ema_weight, void* stream);

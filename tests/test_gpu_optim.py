@@ -440,3 +440,33 @@ def test_deferred_clip_step_equals_eager_clip_step(cuda):
 
     for a, b in zip(run(False), run(True)):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("factor", [2.0 ** 12, 2.0 ** -12, 2.0])
+def test_prescaled_x0_repair(cuda, factor):
+    """The front writes the Gram input as binary16(bf16(u) * k) with k from the
+    previous step's norm. Corrupting the stored k after the first step (2^12:
+    X0 would overflow binary16; 2^-12: it would flush to zero; 2: still in
+    range) must not change the next steps beyond rounding: out-of-range
+    matrices are rewritten with this step's k before the Gram products."""
+    def run(corrupt):
+        model = synth.SyntheticLM(synth.MICRO, device=cuda, seed=0)
+        muon, adamw = build_optimizers(model, muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1,
+                                       cautious_wd=True, bf16_master=True)
+        for k in range(3):
+            synth.set_grads(model, synth.make_grads(model, k, seed=0))
+            muon.step()
+            if k == 0 and corrupt:
+                for ws in muon._ws.values():
+                    ws["prescale"].mul_(factor)
+        torch.cuda.synchronize()
+        assert _lib.device_error() == 0
+        return [p.detach().float().clone() for p in muon.param_groups[0]["params"]], muon
+
+    ref, _ = run(False)
+    got, muon = run(True)
+    for a, b in zip(ref, got):
+        assert torch.isfinite(b).all()
+        assert rel_fro(b, a) < 1e-3
+    if factor != 2.0:  # the corrupted batches were flagged and rewritten at step 1
+        assert any(int(ws["flags"].sum()) == 0 for ws in muon._ws.values())  # step 2 needed no repair

@@ -196,8 +196,8 @@ def test_normuon_param_group_keys_match_reference():
 def test_ctypes_structs_match_header_layout():
     assert ctypes.sizeof(_lib.AdamwTensor) == 6 * 8 + 8 + 4 + 4 + 8
     assert ctypes.sizeof(_lib.AdamwGroup) == 8 * 4 + 8  # 7 floats, cautious flag, grad_scale pointer
-    assert ctypes.sizeof(_lib.NormuonBatch) == 4 * 4 + 11 * 8
-    assert ctypes.sizeof(_lib.OrthoGroup) == 4 * 8 + 4 * 4
+    assert ctypes.sizeof(_lib.NormuonBatch) == 4 * 4 + 14 * 8 + 2 * 4
+    assert ctypes.sizeof(_lib.OrthoGroup) == 4 * 8 + 4 * 4 + 8
 
 
 def test_bf16_newton_schulz_noise_floor():
