@@ -283,6 +283,64 @@ class ShardedStep:
         mark("table_wait")
 
     @torch.no_grad()
+    def reduce_gradients(self, average: bool = True, reduce_dtype=torch.float32):
+        """Data-parallel gradient exchange before the sharded step (each rank
+        computed gradients on its own data): every rank ends with the sum, or
+        the mean, over ranks of the gradients it reads in step() -- its NorMuon
+        matrices (one reduce-scatter over a gradient buffer laid out like the
+        weight arena), its rows of the split tables (one reduce-scatter each)
+        and the small replicated tensors (one all-reduce, packed). Other
+        gradients keep their local values. Sums run in ``reduce_dtype``
+        (fp32 by default: a bf16 sum over two ranks is rounded once) and are
+        rounded to the gradient dtype after the optional division by the world
+        size. Every rank must call it (collectives)."""
+        if self.world == 1:
+            return
+        scale = (1.0 / self.world) if average else None
+        mparams = [p for g in self.muon.param_groups for p in g["params"]]
+        if self.chunk:
+            dev = self.arena.device
+            if getattr(self, "_grad_arena", None) is None or self._grad_arena.dtype != reduce_dtype:
+                self._grad_arena = torch.zeros(self.arena.numel(), dtype=reduce_dtype, device=dev)
+                self._grad_out = torch.empty(self.chunk, dtype=reduce_dtype, device=dev)
+            base = self.arena.data_ptr()
+            es = self.arena.element_size()
+            offs = []
+            for p in mparams:
+                off = (p.data.data_ptr() - base) // es
+                offs.append(off)
+                if p.grad is not None:
+                    self._grad_arena[off:off + p.numel()].copy_(p.grad.view(-1))
+            dist.reduce_scatter_tensor(self._grad_out, self._grad_arena, group=self.group)
+            if scale is not None:
+                self._grad_out.mul_(scale)
+            lo = self.rank * self.chunk
+            for p, off in zip(mparams, offs):
+                if self.owner[id(p)] == self.rank and p.grad is not None:
+                    p.grad.view(-1).copy_(self._grad_out[off - lo:off - lo + p.numel()])
+        for p in self.row_sharded:
+            if p.grad is None:
+                continue
+            flat = p.grad.view(-1)
+            per = flat.numel() // self.world
+            out = torch.empty(per, dtype=reduce_dtype, device=flat.device)
+            dist.reduce_scatter_tensor(out, flat.to(reduce_dtype), group=self.group)
+            if scale is not None:
+                out.mul_(scale)
+            flat[self.rank * per:(self.rank + 1) * per].copy_(out)
+        small = [p for g in self.adamw.param_groups for p in g["params"]
+                 if p.grad is not None and not any(p is t for t in self.row_sharded)]
+        if small:
+            packed = torch.cat([p.grad.reshape(-1).to(reduce_dtype) for p in small])
+            dist.all_reduce(packed, group=self.group)
+            if scale is not None:
+                packed.mul_(scale)
+            off = 0
+            for p in small:
+                p.grad.view(-1).copy_(packed[off:off + p.numel()])
+                off += p.numel()
+
+    @torch.no_grad()
     def gather_state(self):
         """Completes every rank's optimizer state from the owners (for a
         checkpoint in the reference layout; collectives on every rank): the

@@ -27,7 +27,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, exchange, q):
+def _worker(rank, world, port, exchange, q, dp=False):
     import torch.distributed as dist
 
     from sol_b200 import EmaWeights, build_optimizers, synth
@@ -51,9 +51,20 @@ def _worker(rank, world, port, exchange, q):
         rmuon, radamw = build_optimizers(ref, adam_master="bf16_mt", **KW)
         rema = EmaWeights(ref, 0.999)
         for step in range(STEPS):
-            grads = synth.make_grads(model, step, seed=0)
-            synth.set_grads(model, [g.clone() for g in grads])
-            synth.set_grads(ref, grads)
+            if dp:
+                # data parallel: each rank its own gradients; the reference
+                # steps on their mean (an fp32 sum of two bf16 values is exact,
+                # the halving too: one rounding, as in reduce_gradients)
+                mine = synth.make_grads(model, step, seed=rank)
+                both = [synth.make_grads(model, step, seed=r) for r in range(world)]
+                grads = [(sum(g[i].float() for g in both) / world).to(mine[i].dtype) for i in range(len(mine))]
+                synth.set_grads(model, [g.clone() for g in mine])
+                synth.set_grads(ref, grads)
+                sharded.reduce_gradients(average=True)
+            else:
+                grads = synth.make_grads(model, step, seed=0)
+                synth.set_grads(model, [g.clone() for g in grads])
+                synth.set_grads(ref, grads)
             sharded.step()
             rmuon.step()
             radamw.step()
@@ -89,15 +100,17 @@ def _worker(rank, world, port, exchange, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["ce", "hybrid", "nccl"])
-def test_sharded_step_bit_identical_to_single_gpu(exchange):
+@pytest.mark.parametrize("exchange,dp", [("ce", False), ("hybrid", False), ("nccl", False), ("auto", True)])
+def test_sharded_step_bit_identical_to_single_gpu(exchange, dp):
+    """dp: each rank steps on its own gradients after reduce_gradients; the
+    single-GPU reference steps on their mean."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q, dp)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -113,7 +126,7 @@ def test_sharded_step_bit_identical_to_single_gpu(exchange):
     for r in range(world):
         v = out[r]
         assert isinstance(v, dict), (r, v)
-        assert v["exchange"] == exchange
+        assert v["exchange"] == (exchange if exchange != "auto" else "ce")
         assert v["bad"] == [], (r, v["bad"])
         assert v["bad_ema"] == [], (r, v["bad_ema"])
         assert v["bad_state"] == [], (r, v["bad_state"])

@@ -128,3 +128,71 @@ def test_rank_leaving_is_detected_not_hung():
     out = _run(2, "leave")
     assert out[1] == "left"
     assert isinstance(out[0], str) and out[0].startswith("error"), out[0]
+
+
+def _reduce_worker(rank, world, port, average, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        model = synth.SyntheticLM(synth.MICRO, seed=0)
+        muon, adamw = build_optimizers(model, **KW)
+        ema = EmaWeights(model, 0.999)
+        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16)
+        named = list(model.named_parameters())
+        with torch.no_grad():
+            for n, p in named:
+                p.grad = _expected(n + f"#{rank}", p.shape, p.dtype)
+        sharded.reduce_gradients(average=average)
+        worst = 0.0
+        checked = 0
+        for n, p in named:
+            exact = sum(_expected(n + f"#{r}", p.shape, p.dtype).float() for r in range(world))
+            if average:
+                exact = exact / world
+            want = exact.to(p.dtype).float()
+            got = p.grad.float()
+            if id(p) in sharded.owner:
+                if sharded.owner[id(p)] != rank:
+                    continue
+            elif any(p is t for t in sharded.row_sharded):
+                start, cnt = adamw._owned_slices[id(p)]
+                want = want.view(-1)[start:start + cnt]
+                got = got.view(-1)[start:start + cnt]
+            # at most one bf16 rounding step apart (fp32 sums in another order)
+            ulp = torch.clamp(want.abs(), min=1e-30) * 2.0 ** -7
+            worst = max(worst, float(((got - want).abs() / ulp).max()))
+            checked += 1
+        q.put((rank, {"worst_ulps": worst, "checked": checked}))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"error: {type(e).__name__}: {e}"))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,average", [(2, False), (2, True), (3, True)])
+def test_reduce_gradients_sums_what_each_rank_reads(world, average):
+    """Each rank holds its own gradients; after reduce_gradients every rank
+    holds the sum (or mean) over ranks of the gradients its step reads."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, average, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            r, v = q.get(timeout=180)
+            out[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert isinstance(out[r], dict), out[r]
+        assert out[r]["checked"] > 0
+        limit = 0.0 if world == 2 else 1.0  # two addends: one rounding, bit-exact
+        assert out[r]["worst_ulps"] <= limit, out[r]
