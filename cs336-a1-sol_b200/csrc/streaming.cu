@@ -427,9 +427,10 @@ __device__ __forceinline__ void store_u8(uint16_t* dst, const float* u, bool x0,
 // REPAIR = true: rewrites X0 of the matrices flagged by the prescale pass from
 // the gradient and the already updated momentum buffer (no state changes).
 template <typename T, bool REPAIR>
-__device__ __forceinline__ void front_body(const FrontTable& tab, float w_small, float w_large, int nesterov) {
-  const MultiBatchInfo& bi = tab.h.b[find_batch_cta(tab.h, blockIdx.x)];
-  const int local = blockIdx.x - bi.cta0;
+__device__ __forceinline__ void front_body(const FrontTable& tab, int cta, float w_small, float w_large,
+                                           int nesterov) {
+  const MultiBatchInfo& bi = tab.h.b[find_batch_cta(tab.h, cta)];
+  const int local = cta - bi.cta0;
   const int s = local / bi.nparts;
   const int part = local - s * bi.nparts;
   if (REPAIR && (!bi.x0_half || !bi.flags[s])) return;
@@ -496,18 +497,29 @@ template <typename T>
 __global__ void __launch_bounds__(kFrontThreads) normuon_front_kernel(const __grid_constant__ FrontTable tab,
                                                                       float w_small, float w_large, int nesterov) {
   pdl_wait();
-  front_body<T, false>(tab, w_small, w_large, nesterov);
+  front_body<T, false>(tab, blockIdx.x, w_small, w_large, nesterov);
 }
 
+// kRepairCtas CTAs per matrix: an unflagged matrix (almost all of them)
+// costs each CTA one flag load; a flagged one is rewritten by its CTAs.
+constexpr int kRepairCtas = 8;
 template <typename T>
 __global__ void __launch_bounds__(kFrontThreads) normuon_x0_repair_kernel(const __grid_constant__ FrontTable tab,
                                                                           float w_small, float w_large,
                                                                           int nesterov) {
   pdl_wait();
-  front_body<T, true>(tab, w_small, w_large, nesterov);
+  const int m = blockIdx.x / kRepairCtas;
+  const int sub = blockIdx.x - m * kRepairCtas;
+  int kb = 0;
+  while (kb + 1 < tab.h.nb && m >= tab.h.b[kb + 1].mat0) ++kb;
+  const MultiBatchInfo& bi = tab.h.b[kb];
+  const int s = m - bi.mat0;
+  if (!bi.x0_half || !bi.flags[s]) return;
+  for (int part = sub; part < bi.nparts; part += kRepairCtas)
+    front_body<T, true>(tab, bi.cta0 + s * bi.nparts + part, w_small, w_large, nesterov);
 }
 
-// One thread per matrix of the x0_half batches: this step's norm scale, the
+// One warp per matrix of the x0_half batches: this step's norm scale, the
 // factor s_norm / k for the orthogonaliser and next step's k = 2^(8 + e) with
 // s_norm in [2^(e-1), 2^e): ||X0|| ~ 2^8 keeps X0's entries far from both ends
 // of binary16. A matrix whose ||X0|| = k / s_norm left [2^2, 2^14] (or that had
@@ -515,15 +527,19 @@ __global__ void __launch_bounds__(kFrontThreads) normuon_x0_repair_kernel(const 
 __global__ void __launch_bounds__(128) normuon_prescale_kernel(const __grid_constant__ MultiHeader h, int nmats,
                                                                float eps, float safety) {
   pdl_wait();
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (m >= nmats) return;
   int kb = 0;
   while (kb + 1 < h.nb && m >= h.b[kb + 1].mat0) ++kb;
   const MultiBatchInfo& bi = h.b[kb];
   if (!bi.x0_half) return;
   const int s = m - bi.mat0;
-  float acc = 0.f;
-  for (int i = 0; i < bi.nparts; ++i) acc += bi.partial[static_cast<int64_t>(s) * bi.nparts + i];
+  float acc = 0.f;  // lane-strided partial sums, then a fixed-order butterfly
+  for (int i = lane; i < bi.nparts; i += 32) acc += bi.partial[static_cast<int64_t>(s) * bi.nparts + i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane != 0) return;
   const float sn = 1.0f / (sqrtf(acc) * safety + eps);
   int e = 0;
   frexpf(sn, &e);
@@ -613,15 +629,16 @@ static int front_launch(const b2o_normuon_batch* batches, int nb, int dtype, flo
   }
   if (repair) {
     // this step's scales, next step's k, flags; then X0 of the flagged matrices
-    launch_pdl(normuon_prescale_kernel, dim3((nmats + 127) / 128), dim3(128), 0, stream, tab.h, nmats, norm_eps,
-               norm_safety);
+    launch_pdl(normuon_prescale_kernel, dim3((nmats * 32 + 127) / 128), dim3(128), 0, stream, tab.h, nmats,
+               norm_eps, norm_safety);
     count_launch();
     if (int e = check_launch("normuon_prescale")) return e;
+    const int rgrid = nmats * kRepairCtas;
     if (dtype == B2O_F32)
-      launch_pdl(normuon_x0_repair_kernel<float>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small,
+      launch_pdl(normuon_x0_repair_kernel<float>, dim3(rgrid), dim3(kFrontThreads), 0, stream, tab, w_small,
                  w_large, nesterov);
     else
-      launch_pdl(normuon_x0_repair_kernel<uint16_t>, dim3(ncta), dim3(kFrontThreads), 0, stream, tab, w_small,
+      launch_pdl(normuon_x0_repair_kernel<uint16_t>, dim3(rgrid), dim3(kFrontThreads), 0, stream, tab, w_small,
                  w_large, nesterov);
     count_launch();
     return check_launch("normuon_x0_repair");
