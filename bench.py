@@ -24,7 +24,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -57,64 +56,82 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons during the timed region,
+    read through NVML (reads only) every few milliseconds from a thread, so
+    that short timed regions (a sharded step on 8 GPUs takes ~1.5 ms) still
+    get samples. The device is matched by UUID / PCI bus id, not by index."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, index):
+    def __init__(self, index, period_s=0.004):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.period = period_s
+        self.samples = []
+        self.nvml = None
+        self.t0 = 0.0
+
+    def _handle(self, nv):
+        props = torch.cuda.get_device_properties(self.index)
+        uuid = str(getattr(props, "uuid", ""))
+        for cand in (uuid, "GPU-" + uuid):
+            try:
+                return nv.nvmlDeviceGetHandleByUUID(cand.encode() if isinstance(cand, str) else cand)
+            except Exception:  # noqa: BLE001
+                pass
+        try:
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:  # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except FileNotFoundError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nvml = nv
+            self.handle = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM))
+        except Exception as e:  # noqa: BLE001
+            self.nvml = None
+            self.error = f"NVML unavailable: {type(e).__name__}"
+            return
+        self.stop_flag = threading.Event()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append((time.time(), line.strip()))
+        def poll():
+            while not self.stop_flag.is_set():
+                try:
+                    sm = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                    rs = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                    self.samples.append((time.time(), float(sm), int(rs)))
+                except Exception:  # noqa: BLE001
+                    pass
+                self.stop_flag.wait(self.period)
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
 
     def mark(self):
         """Start of the timed region (samples before it are warm-up)."""
         self.t0 = time.time()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        t0 = getattr(self, "t0", 0.0)
-        timed = [ln for t, ln in self.lines if t >= t0]
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [getattr(self, "error", "NVML unavailable")]}
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        timed = [x for x in self.samples if x[0] >= self.t0]
         window = "timed region"
-        if len(timed) < 2:  # very short timed region: include the warm-up samples
-            timed, window = [ln for _, ln in self.lines], "warm-up + timed region"
-        for ln in timed:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm), "window": window}
+        if len(timed) < 2:  # fewer than two polls fell inside: include the warm-up ones
+            timed, window = self.samples, "warm-up + timed region"
+        reasons = sorted({nm for _, _, rs in timed for nm, bit in self.REASONS if rs & bit})
+        sm = [x[1] for x in timed]
+        try:
+            self.nvml.nvmlShutdown()
+        except Exception:  # noqa: BLE001
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm), "window": window, "source": "NVML"}
 
 
 def gram_flops(m, n, T=5, resets=(2,), mode="gram"):
