@@ -82,32 +82,23 @@ int64_t ortho_workspace_bytes(int S, int r, int c) {
   return ortho_workspace_bytes_multi(&g, 1);
 }
 
-// Per-matrix norm of the front's bf16 output, from its partial sums.
-// scal layout: [0, Stot) scale s, [Stot, 2 Stot) s^2, [2 Stot, 3 Stot) quintic divisor;
-// this group's matrices start at s_off.
-__global__ void norm_finalize_kernel(const float* __restrict__ partial, int nparts, int S, int mode, float eps,
-                                     float safety, float* __restrict__ scal, int Stot, int s_off) {
+// Quintic mode: the divisor bf16(bf16(||u||) + eps) of zeropower_via_newtonschulz5
+// (sol_modules.py:283; X.norm() of a bf16 tensor is returned in bf16 and "+ eps"
+// is bf16 arithmetic again), from the front's partial sums in index order.
+// scal[2 Stot + s_off + s]: this group's matrices start at s_off.
+__global__ void quintic_divisor_kernel(const float* __restrict__ partial, int nparts, int S, float eps,
+                                       float* __restrict__ scal, int Stot, int s_off) {
   pdl_wait();
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= S) return;
   float acc = 0.f;
   for (int i = 0; i < nparts; ++i) acc += partial[static_cast<int64_t>(s) * nparts + i];
-  const float nrm = sqrtf(acc);
-  if (mode == 0) {
-    // X.norm() of a bf16 tensor is returned in bf16; "+ eps" is again bf16 arithmetic
-    const float nb = round_bf16(nrm);
-    scal[2 * Stot + s_off + s] = round_bf16(nb + eps);
-  } else {
-    const float sc = 1.0f / (nrm * safety + eps);
-    scal[s_off + s] = sc;
-    scal[Stot + s_off + s] = sc * sc;
-  }
+  scal[2 * Stot + s_off + s] = round_bf16(round_bf16(sqrtf(acc)) + eps);
 }
 
 // Gram mode: X0 = binary16(u * s) for every matrix of every group of a
 // multi-group call in one launch; each CTA derives its matrix's scale
-// s = 1 / (||u|| * safety + eps) from the front's partial sums (summed in the
-// order norm_finalize_kernel uses).
+// s = 1 / (||u|| * safety + eps) from the front's partial sums (in index order).
 constexpr int kToHalfGroups = 16;
 constexpr int64_t kToHalfPart = 256 * 8 * 16;  // elements per CTA
 struct ToHalfGroup {
@@ -251,7 +242,7 @@ __global__ void __launch_bounds__(kSmallThreads) small_gram_ns_kernel(
   const int64_t rc = static_cast<int64_t>(a.r) * a.c;
   pdl_wait();
   // scale s = 1 / (||u|| * safety + eps) from the front's partial sums of u^2
-  if (threadIdx.x == 0) {  // summed in the order norm_finalize_kernel uses
+  if (threadIdx.x == 0) {  // partial sums in index order, as the conversion kernel adds them
     float acc = 0.f;
     for (int i = 0; i < a.nparts; ++i) acc += partial[static_cast<int64_t>(s) * a.nparts + i];
     red[0] = 1.0f / (sqrtf(acc) * a.safety + a.eps);
@@ -493,10 +484,10 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   }
   for (int g = 0; g < ng && mode == 0; ++g) {
     const int nparts = normuon_front_parts(bg[g].rc);
-    launch_pdl(norm_finalize_kernel, dim3((bg[g].S + 127) / 128), dim3(128), 0, stream, groups[g].partial, nparts,
-               bg[g].S, mode, norm_eps, norm_safety, scal, L.Stot, L.s_off[g]);
+    launch_pdl(quintic_divisor_kernel, dim3((bg[g].S + 127) / 128), dim3(128), 0, stream, groups[g].partial, nparts,
+               bg[g].S, norm_eps, scal, L.Stot, L.s_off[g]);
     count_launch();
-    if (int e = check_launch("norm_finalize")) return e;
+    if (int e = check_launch("quintic_divisor")) return e;
   }
 
   int rc_ = 0;
