@@ -42,7 +42,7 @@ MOM_WARMUP = 300
 # dram__bytes_read.sum + dram__bytes_write.sum per tensor-core GEMM launch,
 # averaged over the 30 launches of one L14 step (ncu capture summarised in
 # profiles/gemm_tc_c2_L14_dram_traffic.md); only meaningful for the default config.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.179e8
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.169e8  # profiles/gemm_tc_c2_L14_dram_traffic.md (C2, one GPU)
 
 
 def peaks():

@@ -470,3 +470,24 @@ def test_prescaled_x0_repair(cuda, factor):
         assert rel_fro(b, a) < 1e-3
     if factor != 2.0:  # the corrupted batches were flagged and rewritten at step 1
         assert any(int(ws["flags"].sum()) == 0 for ws in muon._ws.values())  # step 2 needed no repair
+
+
+def test_clip_grad_norm_fp32_gradients(cuda):
+    """fp32 gradients (config C1): norms and coefficient in fp32, where the
+    summation order may differ from torch's in the last bits."""
+    from sol_b200 import clip_grad_norm_
+    model = synth.SyntheticLM(synth.C1, device=cuda, seed=0)
+    grads = synth.make_grads(model, 0, seed=0)
+    params = [p for _, p in model.named_parameters()]
+    for p, g in zip(params, grads):
+        p.grad = g.clone()
+    ref = torch.nn.utils.clip_grad_norm_(params, 1e-3, foreach=True)
+    ref_grads = [p.grad.clone() for p in params]
+    for p, g in zip(params, grads):
+        p.grad = g.clone()
+    got = clip_grad_norm_(params, 1e-3)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    assert abs(float(got) - float(ref)) <= 4e-7 * float(ref)
+    for p, r in zip(params, ref_grads):
+        assert torch.allclose(p.grad, r, rtol=4e-7, atol=0)
