@@ -230,3 +230,33 @@ def test_bf16_newton_schulz_noise_floor():
         alt = ns_f64_acc(G).double()
         errs.append((torch.linalg.norm(ref - alt) / torch.linalg.norm(ref)).item())
     assert max(errs) > 3e-3, errs
+
+
+def test_every_header_symbol_has_a_ctypes_signature():
+    names = set(_header_symbols())
+    assert names == set(_lib.SIGNATURES), sorted(names ^ set(_lib.SIGNATURES))
+
+
+def test_host_validation_of_the_newer_entry_points():
+    """Multi-batch, prescale, clip and peer-exchange calls reject bad
+    arguments on the host with a message (nothing launched, no GPU needed)."""
+    lib = _lib.load()
+    batch = (_lib.NormuonBatch * 1)()
+    assert lib.b2o_normuon_front_multi(batch, 0, 1, 0.05, 0.95, 1, None, None) < 0
+    assert "batches" in _lib.last_error()
+    assert lib.b2o_normuon_front_multi(batch, 1, 1, 0.05, 0.95, 1, None, None) < 0  # S = 0
+    assert "1..64" in _lib.last_error()
+    assert lib.b2o_normuon_prescale(batch, 17, 1, 0.05, 0.95, 1, None, 1e-7, 1.0, None) < 0
+    assert lib.b2o_normuon_apply_multi(batch, 1, 3, -1e-3, 0.0, 1.0, 0, 0, 0.05, 0.0, None) < 0
+    assert "dtype" in _lib.last_error()
+    numels = (ctypes.c_int64 * 1)(10)
+    dtypes = (ctypes.c_int * 1)(5)
+    ptrs = _lib.ptr_array([0])
+    assert lib.b2o_clip_scratch_floats(numels, 0) == -1
+    assert lib.b2o_clip_grad_norm(ptrs, numels, dtypes, 1, 1.0, None, None, None) < 0
+    assert "bad tensor" in _lib.last_error() or "fp32 or bf16" in _lib.last_error()
+    assert lib.b2o_clip_scale(ptrs, numels, dtypes, 2000, None, None) < 0
+    assert lib.b2o_ipc_export(None, None, None) < 0
+    assert lib.b2o_ipc_import(None, None) < 0
+    assert lib.b2o_copy_async(None, None, None, -1, None) < 0
+    assert "copy_async" in _lib.last_error()
