@@ -196,3 +196,31 @@ def test_reduce_gradients_sums_what_each_rank_reads(world, average):
         assert out[r]["checked"] > 0
         limit = 0.0 if world == 2 else 1.0  # two addends: one rounding, bit-exact
         assert out[r]["worst_ulps"] <= limit, out[r]
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_owned_regions_are_disjoint_and_cover_every_update(world):
+    """The regions each rank pushes (sharded step) tile every NorMuon matrix and
+    every row-sharded table exactly once."""
+    steps = []
+    for rank in range(world):
+        model = synth.SyntheticLM(synth.MICRO, seed=0)
+        muon, adamw = build_optimizers(model, **KW)
+        steps.append(ShardedStep(model, muon, adamw, None, world=world, rank=rank, min_rows_shard=16,
+                                 exchange="nccl"))
+    ref = steps[0]
+    bufs = ref.buffers()
+    covered = [torch.zeros(b.numel() * b.element_size(), dtype=torch.int32) for b in bufs]
+    for st in steps:
+        assert [b.numel() for b in st.buffers()] == [b.numel() for b in bufs]
+        for k, off, nbytes in st.owned_regions(st.rank):
+            covered[k][off:off + nbytes] += 1
+    assert all(int(c.max()) <= 1 for c in covered)  # disjoint
+    # every byte of every NorMuon matrix and every table is pushed by one rank
+    base = ref.arena.data_ptr()
+    es = ref.arena.element_size()
+    for p in (p for g in ref.muon.param_groups for p in g["params"]):
+        off = p.data.data_ptr() - base
+        assert int(covered[0][off:off + p.numel() * es].min()) == 1
+    for k in range(1, len(bufs)):
+        assert int(covered[k].min()) == 1
