@@ -151,16 +151,19 @@ def test_mantissa_split_is_bit_exact(cuda):
 
 
 # ----------------------------------------------------------------- NorMuon --
-def _normuon_pair(cfg, steps, cautious, bf16_master, orthogonalizer, coefficients="quintic", wd=0.1):
+def _normuon_pair(cfg, steps, cautious, bf16_master, orthogonalizer, coefficients="quintic", wd=0.1,
+                  nesterov=True, ortho=None, engine_cls=None):
     model_c = synth.SyntheticLM(cfg, seed=0)
     model_g = synth.SyntheticLM(cfg, seed=0).cuda()
     muon_c = [p for n, p in model_c.named_parameters() if n in ref_step.route(model_c.named_parameters())[0]]
     names = ref_step.route(model_c.named_parameters())[0]
     gmap = dict(model_g.named_parameters())
     muon_g = [gmap[n] for n in names]
-    orc = ref_step.RefNorMuon(muon_c, lr=8e-3, weight_decay=wd, cautious_wd=cautious, bf16_master=bf16_master)
-    eng = NorMuonGNS(muon_g, lr=8e-3, weight_decay=wd, cautious_wd=cautious, bf16_master=bf16_master,
-                     orthogonalizer=orthogonalizer, coefficients=coefficients)
+    orc = ref_step.RefNorMuon(muon_c, lr=8e-3, weight_decay=wd, cautious_wd=cautious, bf16_master=bf16_master,
+                              nesterov=nesterov, ortho=ortho)
+    eng = (engine_cls or NorMuonGNS)(muon_g, lr=8e-3, weight_decay=wd, cautious_wd=cautious,
+                                     bf16_master=bf16_master, nesterov=nesterov, orthogonalizer=orthogonalizer,
+                                     coefficients=coefficients)
     p0 = [p.detach().clone().float() for p in muon_c]
     for it in range(steps):
         mom = 0.85 + 0.10 * min(1.0, it / 300)
@@ -491,3 +494,54 @@ def test_clip_grad_norm_fp32_gradients(cuda):
     assert abs(float(got) - float(ref)) <= 4e-7 * float(ref)
     for p, r in zip(params, ref_grads):
         assert torch.allclose(p.grad, r, rtol=4e-7, atol=0)
+
+
+
+def _cumulative_error(pc, pg, p0):
+    du_c = torch.cat([(p.detach().float() - a).reshape(-1) for p, a in zip(pc, p0)])
+    du_g = torch.cat([(p.detach().float().cpu() - a).reshape(-1) for p, a in zip(pg, p0)])
+    return rel_fro(du_g, du_c)
+
+
+def test_normuon_without_nesterov_or_weight_decay(cuda):
+    """nesterov=False (u = buf, sol_modules.py:394) and weight_decay=0 (no decay
+    factor at all) against the oracle, fp32 C1, quintic mode."""
+    names, pc, pg, p0, orc, eng = _normuon_pair(synth.C1, 10, False, False, "quintic", wd=0.0, nesterov=False)
+    err = _cumulative_error(pc, pg, p0)
+    print(f"no nesterov, no wd: cumulative update rel. Frobenius error = {err:.2e}")
+    assert err <= 1e-2
+
+
+def test_normuon_gram_path_vs_fp64_gram_oracle(cuda):
+    """The production path (Gram Newton-Schulz, Polar Express table, binary16,
+    prescaled input written by the front) on fp32 parameters against the
+    oracle's NorMuon step with the fp64 Gram restatement as orthogonaliser."""
+    table = polar_express.polar_express(5)
+
+    def gram64(U, ns_steps):
+        return gram_ns_ref.gram_ns(U, table).to(torch.bfloat16)
+
+    names, pc, pg, p0, orc, eng = _normuon_pair(synth.C1, 10, True, False, "gram", "polar_express", ortho=gram64)
+    err = _cumulative_error(pc, pg, p0)
+    print(f"gram/PE engine vs fp64 Gram oracle step: cumulative update rel. Frobenius error = {err:.2e}")
+    assert err <= 1e-2  # measured 4.3e-3 (binary16 iteration, bf16 input rounding)
+
+
+def test_overridden_orthogonalizer_hook_is_used(cuda):
+    """A subclass overriding _orthogonalize_batch (the reference's benches patch
+    it, scripts/muon_copy_bench.py:84-89) gets the bf16 front output and its
+    result drives the update: with the oracle's own quintic as the hook, the
+    engine's step follows the oracle's to the apply arithmetic's rounding."""
+    class Hooked(NorMuonGNS):
+        calls = 0
+
+        def _orthogonalize_batch(self, U, ns_steps):
+            Hooked.calls += 1
+            assert U.dtype == torch.bfloat16 and U.is_cuda
+            return ref_step.ortho_batch_quintic(U.cpu(), ns_steps).to(U.device)
+
+    names, pc, pg, p0, orc, eng = _normuon_pair(synth.C1, 5, False, False, "gram", engine_cls=Hooked)
+    assert Hooked.calls > 0
+    err = _cumulative_error(pc, pg, p0)
+    print(f"hooked quintic vs oracle: cumulative update rel. Frobenius error = {err:.2e}")
+    assert err <= 1e-3
