@@ -545,3 +545,38 @@ def test_overridden_orthogonalizer_hook_is_used(cuda):
     err = _cumulative_error(pc, pg, p0)
     print(f"hooked quintic vs oracle: cumulative update rel. Frobenius error = {err:.2e}")
     assert err <= 1e-3
+
+
+@pytest.mark.parametrize("mode", ["quintic", "gram"])
+def test_normuon_ragged_shapes_and_batch_split(cuda, mode):
+    """70 same-shape matrices (batches of 64 + 6), odd shapes that take the
+    scalar and CUDA-core paths, a 5 x 300 matrix (small-matrix path) and a
+    parameter without gradient (skipped, sol_modules.py:378-379), against the
+    oracle's step (quintic, or the fp64 Gram restatement for gram mode)."""
+    g = torch.Generator().manual_seed(5)
+    shapes = [(24, 40)] * 70 + [(97, 61)] * 3 + [(61, 97)] * 2 + [(5, 300)] + [(33, 33)]
+    base = [torch.randn(s, generator=g) * 0.02 for s in shapes]
+    pc = [torch.nn.Parameter(b.clone()) for b in base]
+    pg = [torch.nn.Parameter(b.clone().cuda()) for b in base]
+    table = polar_express.polar_express(5)
+    ortho = (lambda U, ns: gram_ns_ref.gram_ns(U, table).to(torch.bfloat16)) if mode == "gram" else None
+    orc = ref_step.RefNorMuon(pc, lr=8e-3, weight_decay=0.1, cautious_wd=True, ortho=ortho)
+    eng = NorMuonGNS(pg, lr=8e-3, weight_decay=0.1, cautious_wd=True, orthogonalizer=mode,
+                     coefficients="polar_express" if mode == "gram" else "quintic")
+    for it in range(3):
+        for i, (a, b) in enumerate(zip(pc, pg)):
+            if i == len(shapes) - 1:  # the last parameter never gets a gradient
+                a.grad = b.grad = None
+                continue
+            gr = torch.randn(a.shape, generator=g) * 1e-3
+            a.grad = gr
+            b.grad = gr.cuda()
+        orc.step()
+        eng.step()
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(pg[-1].detach().cpu(), base[-1])  # no gradient: untouched
+    assert "momentum_buffer" not in eng.state.get(pg[-1], {})
+    err = _cumulative_error(pc[:-1], pg[:-1], base[:-1])
+    print(f"{mode}: ragged/split cumulative update rel. Frobenius error = {err:.2e}")
+    assert err <= 1e-2
