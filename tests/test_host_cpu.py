@@ -39,6 +39,27 @@ def test_c2_routing_counts():
     assert all(p.numel() < 100_000 for p in norm)
 
 
+def test_build_optimizers_groups_as_the_reference_checks_them():
+    """The routing assertions of the reference's scripts/verify_ve_gates.py:58-76,
+    on the engine's build_optimizers: per-head value-embedding gate weights go to
+    AdamW without weight decay, the value-embedding table group uses betas
+    (0.75, 0.95), and every group keeps its base_lr (sol_modules.py:480-482)."""
+    from sol_b200 import build_optimizers
+    model = synth.SyntheticLM(synth.MICRO, seed=0)
+    muon, adamw = build_optimizers(model, muon_lr=1e-3, adam_lr=3e-3, embed_lr=6e-3, weight_decay=0.1, ve_lr=None)
+    muon_ids = {id(p) for g in muon.param_groups for p in g["params"]}
+    gate_w = [p for n, p in model.named_parameters() if "_ve_gate_w" in n]
+    vet = {id(p) for n, p in model.named_parameters() if "value_embeds_k" in n}
+    assert gate_w and not any(id(p) in muon_ids for p in gate_w)
+    ve_grp = [g for g in adamw.param_groups if any(id(p) in vet for p in g["params"])]
+    assert ve_grp and tuple(ve_grp[0]["betas"]) == (0.75, 0.95)
+    gate_ids = {id(p) for p in gate_w}
+    gate_grp = [g for g in adamw.param_groups if any(id(p) in gate_ids for p in g["params"])]
+    assert gate_grp and gate_grp[0]["weight_decay"] == 0.0
+    assert muon.param_groups[0]["base_lr"] == 1e-3
+    assert all("base_lr" in g for g in adamw.param_groups)
+
+
 # ----------------------------------------------------------- coefficients --
 def test_polar_express_table_properties():
     table = polar_express.polar_express(5)
