@@ -281,3 +281,17 @@ def test_host_validation_of_the_newer_entry_points():
     assert lib.b2o_ipc_import(None, None) < 0
     assert lib.b2o_copy_async(None, None, None, -1, None) < 0
     assert "copy_async" in _lib.last_error()
+
+
+def test_install_rebinds_the_reference_names():
+    """sol_b200.install(module) puts the engine's build_optimizers, NorMuonGNS
+    and EmaWeights where train_sol.py looks them up (transformer_lm.sol_modules)."""
+    import types
+
+    import sol_b200
+    fake = types.ModuleType("sol_modules_stand_in")
+    fake.build_optimizers = fake.NorMuonGNS = fake.EmaWeights = None
+    assert sol_b200.install(fake) is fake
+    assert fake.build_optimizers is sol_b200.build_optimizers
+    assert fake.NorMuonGNS is sol_b200.NorMuonGNS
+    assert fake.EmaWeights is sol_b200.EmaWeights
