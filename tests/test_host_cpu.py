@@ -197,6 +197,9 @@ def test_no_cpu_fallback():
     m = torch.nn.Linear(4, 4)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         EmaWeights(m).update()
+    from sol_b200 import clip_grad_norm_
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        clip_grad_norm_([p], 1.0)
 
 
 def test_adamw_state_dict_layout_matches_torch():
