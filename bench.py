@@ -40,9 +40,10 @@ from sol_b200.sharding import ShardedStep  # noqa: E402
 RECIPE = dict(muon_lr=8e-3, adam_lr=1.2e-2, embed_lr=2.4e-2, weight_decay=0.1, cautious_wd=True, bf16_master=True)
 MOM_WARMUP = 300
 # dram__bytes_read.sum + dram__bytes_write.sum per tensor-core GEMM launch,
-# averaged over the 30 launches of one L14 step (ncu capture summarised in
-# profiles/gemm_tc_c2_L14_dram_traffic.md); only meaningful for the default config.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.169e8  # profiles/gemm_tc_c2_L14_dram_traffic.md (C2, one GPU)
+# averaged over the 30 launches of one L14 step, from a one-pass ncu capture
+# of this benchmark's default configuration on one GPU (not measured by the
+# run that prints it; reported for that configuration only).
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.169e8
 
 
 def peaks():
@@ -154,14 +155,16 @@ def gram_flops(m, n, T=5, resets=(2,), mode="gram"):
     return f + 2 * m * m * n  # out = Q X
 
 
-def step_flops(model, muon, mode):
+def step_flops(model, muon, mode, min_m=1):
+    """Orthogonaliser FLOPs of one step over this rank's matrices with min(r, c) >= min_m."""
     tot = 0
     for g in muon.param_groups:
         for p in g["params"]:
             if muon._owned is not None and id(p) not in muon._owned:
                 continue
             r, c = p.shape
-            tot += gram_flops(min(r, c), max(r, c), mode=mode)
+            if min(r, c) >= min_m:
+                tot += gram_flops(min(r, c), max(r, c), mode=mode)
     return tot
 
 
@@ -357,28 +360,27 @@ def engine_arm(args, world, rank, local):
     torch.cuda.synchronize()
     launches = _lib.launch_count() - launches0
     clocks = sampler.stop()
-    # Dominant kernel: every tensor-core GEMM launch bracketed by CUDA events on
-    # its stream, over a second timed run of the same steps (kept apart from the
-    # step timing above because events between launches stop consecutive
-    # kernels from overlapping their launch with the previous one's tail).
-    # The same run also brackets the orthogonaliser calls and the AdamW pass
-    # (phase breakdown).
+    # Phase timing: a second timed run of the same steps with CUDA events on
+    # the launching stream around each orthogonaliser call and the AdamW pass.
+    # The events sit between library calls, not between the GEMM launches of
+    # one call, so the GEMM chain keeps its programmatic dependent launches.
+    # The dominant kernel's figure is the tensor-core GEMM chain: the calls of
+    # the m > 32 classes, whose launches are all tcgen05 GEMMs in the default
+    # Gram mode (the m <= 32 gates run in one CUDA-core kernel of their own).
     torch.cuda.synchronize()
-    _lib.gemm_timing(True)
-    _lib.gemm_timing_read()
     muon._timing_events = ortho_events
     for k in range(args.steps):
         one_step(args.warmup + args.steps + k, record=True)
     torch.cuda.synchronize()
     muon._timing_events = None
-    gemm_ms, gemm_flops, gemm_n = _lib.gemm_timing_read()
-    _lib.gemm_timing(False)
     err = _lib.device_error()
     if err:
         raise RuntimeError(f"device error word {err}")
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world, dev)
-    ortho_ms = sum(a.elapsed_time(b) for a, b in ortho_events) / args.steps
+    ortho_ms = sum(a.elapsed_time(b) for a, b, _, _ in ortho_events) / args.steps
+    gemm_ms = sum(a.elapsed_time(b) for a, b, m, _ in ortho_events if m > 32) / args.steps
+    gemm_n = sum(n for _, _, m, n in ortho_events if m > 32) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in adam_ev) / args.steps
     shard_phases = {}
     for marks in shard_marks:
@@ -388,10 +390,18 @@ def engine_arm(args, world, rank, local):
         adam_ms = shard_phases["adamw"]
     mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
     flops = step_flops(model, muon, mode)
-    peak_burst, peak_tf, peak_gbs, peak_kind = peaks()
-    # dominant kernel: the tensor-core GEMM, timed per launch with CUDA events
-    # on its stream inside the timed region; FLOPs are each launch's algorithmic
-    # count (symmetric outputs at half)
+    gemm_flops = step_flops(model, muon, mode, min_m=33)
+    peak_burst, peak_sus, peak_gbs, peak_kind = peaks()
+    # dominant kernel: the tensor-core GEMM chain, algorithmic FLOPs (symmetric
+    # outputs at half) over its device time in the step. Denominator: the burst
+    # bf16 peak when the SM clock held its maximum through the timed region,
+    # the sustained (power-capped) one when the clock samples show it lowered.
+    sm, smax = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    at_max = bool(sm and smax and sm >= 0.97 * smax)
+    peak_tf = peak_burst if at_max or not sm else peak_sus
+    peak_label = (f"{peak_kind} bf16 burst (SM clock median {sm} of max {smax} MHz in the timed region)"
+                  if peak_tf == peak_burst else
+                  f"{peak_kind} bf16 sustained (SM clock median {sm} of max {smax} MHz: power-capped)")
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     # AdamW+EMA streaming bytes: p 2+2, rem 2+2, g 2, m 4+4, v 4+4, fp32 EMA 4+4 = 34 B/elem
     adam_elems = sum(p.numel() for g in adamw.param_groups for p in g["params"])
@@ -421,11 +431,15 @@ def engine_arm(args, world, rank, local):
                      "frac": (achieved / peak_tf) if achieved else None,
                      "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH if (args.config == "c2_L14_d1024" and world == 1)
                      else None,
-                     "launches_per_step": gemm_n / args.steps, "gemm_ms_per_step": gemm_ms / args.steps,
+                     "traffic_source": "ncu one-pass capture of this configuration's GEMM launches (DRAM read + "
+                                       "write per launch), not measured by this run",
+                     "launches_per_step": gemm_n, "gemm_ms_per_step": gemm_ms, "flops_per_step": gemm_flops,
                      "flops_per_launch": gemm_flops / max(1, gemm_n),
-                     "peak_kind": f"{peak_kind} bf16 sustained (the GEMMs run inside a continuous step loop "
-                                  "under the power cap)",
-                     "frac_of_burst_peak": (achieved / peak_burst) if achieved else None},
+                     "timing": "CUDA events on the launching stream around the orthogonaliser calls of the "
+                               "tensor-core classes (30 GEMM launches each, nothing else), second timed run",
+                     "peak_kind": peak_label,
+                     "frac_of_burst_peak": (achieved / peak_burst) if achieved else None,
+                     "frac_of_sustained_peak": (achieved / peak_sus) if achieved else None},
         "orthogonalizer": {"ms_per_step": ortho_ms, "flops_per_step": flops,
                            "tflops": flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None},
         "host_enqueue_ms_per_step": host_t * 1e3 / args.steps,
@@ -433,11 +447,86 @@ def engine_arm(args, world, rank, local):
     }
     if e2e:
         line["e2e"] = e2e
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg)
     if sharded is not None:
         sharded.close()
     return line
+
+
+def single_gpu_extras(args, cfg, dev):
+    """Measurements printed beside the N = 1 headline, each outside the engine's
+    timed regions: BASELINE configs[2] (Gram-NS TFLOP/s per shape) and
+    configs[3] (AdamW+EMA GB/s) through the engine, and the reference's own
+    optimizer step executed by torch on the same GPU (its quintic fallback:
+    the gram-newton-schulz package it would import is absent, so its GNS path
+    cannot run; the step is the reference's math, bit-exact with it on the CPU)."""
+    out = {}
+    if not args.no_micro:
+        ns = argparse.Namespace(shape="1024x1024,3072x1024,5632x1024,1024x5632", steps=10, warmup=3,
+                                orthogonalizer=args.orthogonalizer, coefficients=args.coefficients, tables=7)
+        g = micro_gram(ns, dev)
+        out["gram_ns_micro"] = {"per_shape": g["per_shape"], "peak": g["peak"], "peak_kind": g["peak_kind"]}
+        torch.cuda.empty_cache()
+        a = micro_adamw(ns, dev)
+        out["adamw_micro"] = {"gbs": a["value"], "ms": a["ms_per_step"], "frac": a["roofline"]["frac"],
+                              "elements": a["config"]["elements"], "bytes_per_element": 34}
+        torch.cuda.empty_cache()
+    if not args.no_reference_gpu:
+        steps, warm = 5, 2
+        ms, _ = run_oracle_steps(cfg, "cuda", steps, warm)
+        out["reference_gpu"] = {"ms": ms, "steps": steps, "warmup": warm, "gns_installed": False,
+                                "orthogonalizer": "quintic fallback (zeropower_via_newtonschulz5, torch bf16 "
+                                                  "matmul on cuBLAS)",
+                                "timing": "median of host-synchronised steps, after the engine's timed regions"}
+        torch.cuda.empty_cache()
+    return out
+
+
+def sharded_parity(args, cfg, world, rank, dev, steps=3):
+    """Bit-identity of the sharded step with the single-GPU engine, checked on
+    every rank after the timed regions: a fresh sharded engine and a fresh
+    unsharded one on the same seeded parameters and gradients take the same
+    steps; every parameter and (after gather_ema) every EMA shadow must be
+    equal bit for bit on every rank. Every rank takes the same collectives."""
+    import torch.distributed as dist
+    kw = dict(orthogonalizer=args.orthogonalizer, coefficients=args.coefficients, adam_master="bf16_mt", **RECIPE)
+    model = synth.SyntheticLM(cfg, device=dev, seed=0)
+    muon, adamw = build_optimizers(model, **kw)
+    ema = EmaWeights(model, 0.999)
+    sh = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, exchange=args.exchange,
+                     push_streams=args.push_streams)
+    ref = synth.SyntheticLM(cfg, device=dev, seed=0)
+    rmuon, radamw = build_optimizers(ref, **kw)
+    rema = EmaWeights(ref, 0.999)
+    try:
+        for it in range(steps):
+            mom = 0.85 + 0.10 * min(1.0, it / MOM_WARMUP)
+            for opt in (muon, rmuon):
+                for g in opt.param_groups:
+                    g["momentum"] = mom
+            grads = synth.make_grads(model, it, seed=0)
+            synth.set_grads(model, [g.clone() for g in grads])
+            synth.set_grads(ref, grads)
+            del grads
+            sh.step()
+            rmuon.step()
+            radamw.step()
+            rema.update()
+        torch.cuda.synchronize()
+        named, rnamed = list(model.named_parameters()), list(ref.named_parameters())
+        bad_p = sum(0 if torch.equal(p.data, r.data) else 1 for (_, p), (_, r) in zip(named, rnamed))
+        sh.gather_ema()
+        torch.cuda.synchronize()
+        bad_e = sum(0 if torch.equal(a, b) else 1 for a, b in zip(ema.shadow, rema.shadow))
+        err = _lib.device_error()
+    finally:
+        sh.close()
+    t = torch.tensor([bad_p, bad_e, 1 if err else 0], dtype=torch.int64, device=dev)
+    dist.all_reduce(t)
+    bad_p, bad_e, errs = (int(x) for x in t.tolist())
+    return {"equal": bad_p == 0 and bad_e == 0 and errs == 0, "mismatched_params": bad_p,
+            "mismatched_ema": bad_e, "ranks_with_device_error": errs, "steps": steps,
+            "checked": f"{len(named)} parameters and EMA shadows on each of {world} ranks, bitwise, against "
+                       "the unsharded engine on the same GPU"}
 
 
 def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, dev, grad_offsets):
@@ -522,34 +611,35 @@ def micro_gram(args, dev):
     from sol_b200 import NorMuonGNS
     shapes = [tuple(int(x) for x in s.split("x")) for s in args.shape.split(",")]
     peak_tf, _, _, peak_kind = peaks()  # kernels timed alone: burst peak
+    S = int(getattr(args, "batch", 14))
     out = []
     for (r, c) in shapes:
         g = torch.Generator(device=dev).manual_seed(0)
-        U = torch.randn(14, r, c, generator=g, device=dev)
+        U = torch.randn(S, r, c, generator=g, device=dev)
         U = U / torch.linalg.matrix_norm(U, ord=2, keepdim=True)
         U = U.to(torch.bfloat16)
         opt = NorMuonGNS([torch.nn.Parameter(torch.zeros(r, c, device=dev))], orthogonalizer=args.orthogonalizer,
                          coefficients=args.coefficients)
         o = torch.empty_like(U)
-        ws = opt._workspace(dev, 14, r, c)
-        part = ws["partial"].view(14, -1)
+        ws = opt._workspace(dev, S, r, c)
+        part = ws["partial"].view(S, -1)
         part.zero_()
         part[:, 0] = U.float().pow(2).sum(dim=(1, 2))
         for _ in range(args.warmup):
-            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
+            opt._ortho(U, ws["partial"], S, r, c, 5, o, ws)
         torch.cuda.synchronize()
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record()
         for _ in range(args.steps):
-            opt._ortho(U, ws["partial"], 14, r, c, 5, o, ws)
+            opt._ortho(U, ws["partial"], S, r, c, 5, o, ws)
         s1.record()
         torch.cuda.synchronize()
         ms = s0.elapsed_time(s1) / args.steps
         mode = "quintic" if args.orthogonalizer == "quintic" else "gram"
-        fl = 14 * gram_flops(min(r, c), max(r, c), mode=mode)
+        fl = S * gram_flops(min(r, c), max(r, c), mode=mode)
         tf = fl / (ms * 1e-3) / 1e12
-        out.append({"shape": f"14x{r}x{c}", "ms": ms, "tflops": tf, "frac": tf / peak_tf})
+        out.append({"shape": f"{S}x{r}x{c}", "ms": ms, "tflops": tf, "frac": tf / peak_tf})
     return {"metric": "Gram-NS TFLOP/s", "value": statistics.mean(x["tflops"] for x in out), "unit": "TFLOP/s",
             "higher_is_better": True, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16/f16",
             "data": "synthetic", "config": {"workload": "configs[2] Gram-NS microbenchmark",
@@ -618,10 +708,14 @@ def main():
     ap.add_argument("--push-streams", type=int, default=1, help="N>1: streams the copy-engine pushes use")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-micro", action="store_true", help="N=1: skip the configs[2]/[3] micro-benchmarks")
+    ap.add_argument("--no-reference-gpu", action="store_true", help="N=1: skip the reference step on the GPU")
+    ap.add_argument("--no-parity", action="store_true", help="N>1: skip the bit-identity check")
     ap.add_argument("--micro", choices=["gram", "adamw"], default=None,
                     help="run a BASELINE micro-benchmark (configs[2] / configs[3]) instead of the full step")
     ap.add_argument("--shape", default="1024x1024,3072x1024,5632x1024,1024x5632")
     ap.add_argument("--tables", type=int, default=7, help="--micro adamw: number of 32768x1024 tables")
+    ap.add_argument("--batch", type=int, default=14, help="--micro gram: matrices per shape")
     args = ap.parse_args()
     if args.device is None:
         args.device = "cuda" if args.impl == "engine" else "cpu"
@@ -645,6 +739,15 @@ def main():
             line = reference_arm(args, world, rank)
         else:
             line = engine_arm(args, world, rank, local)
+            cfg = synth.CONFIGS[args.config]
+            dev = torch.device("cuda", local)
+            torch.cuda.empty_cache()
+            if world > 1 and not args.no_parity:
+                line["parity_vs_single_gpu"] = sharded_parity(args, cfg, world, rank, dev)
+            if world == 1:
+                line.update(single_gpu_extras(args, cfg, dev))
+                if not args.no_cpu_baseline:
+                    line["cpu_baseline"] = cpu_baseline(cfg)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -170,7 +170,7 @@ int b2o_orthogonalize_multi(const b2o_ortho_group* groups, int ngroups, int mode
 }
 
 int64_t b2o_normuon_apply_scratch_floats(int S, int r) {
-  return static_cast<int64_t>(S) * (r + 4);
+  return static_cast<int64_t>(S) * (static_cast<int64_t>(r) + 4);
 }
 
 int b2o_normuon_apply(const uint16_t* d_o, const float* d_rowsq, int S, int r, int c, void* const* params,

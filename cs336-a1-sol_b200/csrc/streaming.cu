@@ -913,7 +913,9 @@ int normuon_apply(const uint16_t* O, const float* rowsq, int S, int r, int c, vo
 // Scratch of b2o_normuon_apply_static: file-scope device memory, reserved by
 // every GPU that loads the library (1 MiB each) for the life of the process.
 // Its address is taken once per device with cudaGetSymbolAddress (the array's
-// name in host code is only a stand-in for the symbol, never a device address).
+// name in host code is only a stand-in for the symbol, never a device address)
+// and cached for the life of that device's primary context: a process that
+// resets the device (cudaDeviceReset) must not call this entry point again.
 constexpr int64_t kStaticApplyScratchFloats = int64_t(1) << 18;
 static __device__ __align__(256) float g_static_apply_scratch[kStaticApplyScratchFloats];
 
@@ -928,7 +930,7 @@ int normuon_apply_static(const uint16_t* O, const float* rowsq, int S, int r, in
                          float neg_lr, float lr_wd, float wd_factor, int wd_on, int cautious, float shape_scale,
                          float w_beta2, float ema_weight, cudaStream_t stream) {
   if (S <= 0 || r <= 0) { set_error("normuon_apply_static: bad args"); return -1; }
-  const int64_t need = static_cast<int64_t>(S) * (r + 4);
+  const int64_t need = static_cast<int64_t>(S) * (static_cast<int64_t>(r) + 4);
   if (need > kStaticApplyScratchFloats) {
     set_error("normuon_apply_static: needs " + std::to_string(need) + " scratch floats (S*(r+4)); the static " +
               "scratch holds " + std::to_string(kStaticApplyScratchFloats) + "; split the batch or use " +

@@ -49,6 +49,7 @@ class AdamW(torch.optim.Optimizer):
         self._ema = None           # EmaWeights folded into the pass (set when it arms)
         self._ema_weight = 0.0
         self._grad_scale = None    # device fp32 clip coefficient for the next step (clip_grad_norm_ defer_to)
+        self._plan = None          # cached launch descriptors (see step)
         register_optimizer(self)
 
     def _init_state(self, p):
@@ -71,55 +72,40 @@ class AdamW(torch.optim.Optimizer):
         in master mode; torch's loader would cast them to bf16)."""
         from .normuon import _load_state_keep_dtypes
         _load_state_keep_dtypes(self, state_dict)
+        self._plan = None
         for group in self.param_groups:
             for p in group["params"]:
                 st = self.state.get(p)
                 if st and "step" in st:
                     self._steps[id(p)] = int(float(st["step"].item()))
 
-    @torch.no_grad()
-    def step(self, closure=None):
-        loss = None
-        if closure is not None:
-            with torch.enable_grad():
-                loss = closure()
-        lib = _lib.load()
-        # bucket by (device, param dtype, state dtype): one kernel launch each
+    def invalidate_plan(self) -> None:
+        """Drops the cached launch descriptors (rebuilt on the next step). Needed
+        only after replacing a parameter's state dict or one of its state
+        tensors by hand (load_state_dict does this itself); steps detect new
+        parameters, moved parameter storage, gradients appearing or vanishing,
+        EMA folding and shard changes themselves."""
+        self._plan = None
+
+    def _build_plan(self, ps, gis, key):
+        """Launch descriptors for the parameters (with gradients) of this step:
+        one b2o_adamw_tensor array per (device, param dtype, state dtype)
+        bucket, with every pointer except the gradient's filled in."""
         buckets = {}
-        gtab = []
-        for gi, group in enumerate(self.param_groups):
-            if gi >= MAX_GROUPS:
-                raise ValueError("at most 8 param groups")
-            b1, b2 = group["betas"]
-            gparams = [p for p in group["params"] if p.grad is not None]
-            if not gparams:
-                gtab.append(None)
-                continue
-            steps = set()
-            for p in gparams:
-                _lib.require_cuda(p, "AdamW.step")
-                if p.grad.dtype != p.dtype or not p.is_contiguous() or not p.grad.is_contiguous():
-                    raise ValueError("AdamW needs contiguous params and grads of the param dtype")
-                st = self._init_state(p)
-                self._steps[id(p)] = self._steps.get(id(p), 0) + 1
-                steps.add(self._steps[id(p)])
-                key = (p.device, p.dtype, st["exp_avg"].dtype)
-                buckets.setdefault(key, []).append((p, st, gi))
-            if len(steps) != 1:
+        step_of = {}
+        for gi, p in zip(gis, ps):
+            _lib.require_cuda(p, "AdamW.step")
+            if not p.is_contiguous():
+                raise ValueError("AdamW needs contiguous params and grads of the param dtype")
+            st = self._init_state(p)
+            if step_of.setdefault(gi, self._steps.get(id(p), 0)) != self._steps.get(id(p), 0):
                 raise RuntimeError("params of one group have different step counts")
-            lr, wd = float(group["lr"]), float(group["weight_decay"])
-            # torch's fused kernel multiplies fp32(lr) * fp32(weight_decay)
-            lr_wd = float(C.c_float(float(C.c_float(lr).value) * float(C.c_float(wd).value)).value)
-            gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
-            gtab.append(_lib.AdamwGroup(lr, float(b1), float(b2), float(group["eps"]), wd, lr_wd,
-                                        float(steps.pop()), int(bool(self.cautious_wd)), gs))
-        groups = (_lib.AdamwGroup * max(1, len(gtab)))()
-        for i, g in enumerate(gtab):
-            if g is not None:
-                groups[i] = g
-        for (dev, pdt, sdt), items in buckets.items():
-            descs = []
-            for p, st, gi in items:
+            buckets.setdefault((p.device, p.dtype, st["exp_avg"].dtype), []).append((gi, p, st))
+        launches, slots, ema_idx = [], [None] * len(ps), set()
+        pos = {id(p): i for i, p in enumerate(ps)}
+        for (dev, pdt, sdt), members in buckets.items():
+            descs, owners = [], []
+            for gi, p, st in members:
                 shadow = self._ema._lookup(p) if self._ema is not None else None
                 rem = st.get("mant_rem")
                 start, n = 0, p.numel()
@@ -133,21 +119,83 @@ class AdamW(torch.optim.Optimizer):
                 descs.append(_lib.AdamwTensor(
                     p.data_ptr() + start * esz,
                     (rem.data_ptr() + start * 2) if rem is not None else None,
-                    p.grad.data_ptr() + start * esz,
+                    None,
                     st["exp_avg"].data_ptr() + start * ssz,
                     st["exp_avg_sq"].data_ptr() + start * ssz,
                     (shadow.data_ptr() + start * 4) if shadow is not None else None,
                     n, gi, 0, st["step"].data_ptr()))
+                owners.append((p, start * esz))
+                if shadow is not None:
+                    ema_idx.add(self._ema._index[id(p)])
             if not descs:
                 continue
-            if self._ema is not None:
-                for p, st, gi in items:
-                    if self._ema._lookup(p) is not None and (
-                            self._owned_slices is None or id(p) in self._owned_slices):
-                        self._ema._mark(p)
             arr = (_lib.AdamwTensor * len(descs))(*descs)
-            rc = lib.b2o_adamw_step(arr, len(descs), groups, len(gtab), _lib.dtype_code(pdt),
-                                    _lib.dtype_code(sdt), self._ema_weight, _lib.stream_ptr(dev))
+            for i, (p, off) in enumerate(owners):
+                slots[pos[id(p)]] = (arr, i, off)
+            launches.append((arr, len(descs), _lib.dtype_code(pdt), _lib.dtype_code(sdt), _lib.stream_ptr(dev)))
+        by_group = {}
+        for gi, p in zip(gis, ps):
+            by_group.setdefault(gi, []).append(id(p))
+        return {"key": key, "ema": self._ema, "owned": self._owned_slices, "state": self.state,
+                "keep": ps, "launches": launches, "slots": slots, "groups": by_group,
+                "ema_idx": frozenset(ema_idx)}
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        lib = _lib.load()
+        ps, gs_, gis = [], [], []
+        for gi, group in enumerate(self.param_groups):
+            if gi >= MAX_GROUPS:
+                raise ValueError("at most 8 param groups")
+            for p in group["params"]:
+                g = p.grad
+                if g is not None:
+                    if g.dtype != p.dtype or not g.is_contiguous():
+                        raise ValueError("AdamW needs contiguous params and grads of the param dtype")
+                    ps.append(p)
+                    gs_.append(g)
+                    gis.append(gi)
+        # The launch descriptors depend only on which parameters step, where
+        # their storage and state live, the EMA folding and the shard: cached
+        # across steps; the gradient pointers are written into them each step.
+        key = (tuple(gis), tuple(map(id, ps)), tuple([p.data_ptr() for p in ps]), len(self.state))
+        plan = self._plan
+        if (plan is None or plan["key"] != key or plan["ema"] is not self._ema or plan["owned"] is not
+                self._owned_slices or plan["state"] is not self.state):
+            plan = self._plan = self._build_plan(ps, gis, key)
+        for slot, g in zip(plan["slots"], gs_):
+            if slot is not None:
+                arr, i, off = slot
+                arr[i].grad = g.data_ptr() + off
+        steps_of = {}
+        for gi, ids in plan["groups"].items():
+            k = self._steps.get(ids[0], 0) + 1
+            self._steps.update(dict.fromkeys(ids, k))
+            steps_of[gi] = k
+        gtab = []
+        gsc = self._grad_scale.data_ptr() if self._grad_scale is not None else None
+        for gi, group in enumerate(self.param_groups):
+            if gi not in steps_of:
+                gtab.append(None)
+                continue
+            b1, b2 = group["betas"]
+            lr, wd = float(group["lr"]), float(group["weight_decay"])
+            # torch's fused kernel multiplies fp32(lr) * fp32(weight_decay)
+            lr_wd = float(C.c_float(float(C.c_float(lr).value) * float(C.c_float(wd).value)).value)
+            gtab.append(_lib.AdamwGroup(lr, float(b1), float(b2), float(group["eps"]), wd, lr_wd,
+                                        float(steps_of[gi]), int(bool(self.cautious_wd)), gsc))
+        groups = (_lib.AdamwGroup * max(1, len(gtab)))()
+        for i, g in enumerate(gtab):
+            if g is not None:
+                groups[i] = g
+        for arr, n, pdt, sdt, stream in plan["launches"]:
+            rc = lib.b2o_adamw_step(arr, n, groups, len(gtab), pdt, sdt, self._ema_weight, stream)
             _lib.check(rc, "adamw_step")
+        if self._ema is not None and plan["ema_idx"]:
+            self._ema._folded |= plan["ema_idx"]
         self._grad_scale = None
         return loss

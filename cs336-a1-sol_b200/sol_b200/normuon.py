@@ -76,8 +76,11 @@ class NorMuonGNS(torch.optim.Optimizer):
         self._owned = None         # set of id(param) this rank updates (sharded step), None = all
         self._ema = None           # EmaWeights folded into the apply pass (set when it arms)
         self._ema_weight = 0.0
-        self._timing_events = None  # list -> (start, end) CUDA events around each orthogonalisation
+        # list -> (start event, end event, m, library launches) around each
+        # orthogonaliser call (benchmark phase timing); None = off
+        self._timing_events = None
         self._grad_scale = None    # device fp32 clip coefficient for the next step (clip_grad_norm_ defer_to)
+        self._plans = {}           # param-group index -> cached launch descriptors (see step)
         register_optimizer(self)
 
     # ------------------------------------------------------------------ hooks
@@ -156,6 +159,7 @@ class NorMuonGNS(torch.optim.Optimizer):
         parameter dtype, which would turn the fp32 v_row of bf16 matrices into
         bf16)."""
         _load_state_keep_dtypes(self, state_dict)
+        self._plans = {}
 
     def _hook_overridden(self):
         return ("_orthogonalize_batch" in self.__dict__ or
@@ -251,13 +255,14 @@ class NorMuonGNS(torch.optim.Optimizer):
         if ev is not None:
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record()
+            n0 = _lib.launch_count()
         rc = lib.b2o_orthogonalize_multi(groups, len(batches), mode, coeffs, ns_steps, resets, nres, self.norm_eps,
                                          self.norm_safety, ortho.data_ptr(), ortho.numel(), _lib.stream_ptr(dev))
         _lib.check(rc, "orthogonalize_multi")
         if ev is not None:
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()
-            ev.append((e0, e1))
+            ev.append((e0, e1, min(batches[0]["r"], batches[0]["c"]), _lib.launch_count() - n0))
 
     def _apply_all(self, recs, group):
         """v_row, normalisation, shape scale, cautious WD, update, mantissa split and
@@ -297,6 +302,8 @@ class NorMuonGNS(torch.optim.Optimizer):
             _lib.check(rc, "normuon_apply")
 
     def _step_group(self, batches, group):
+        """One parameter group through the per-step code path (used when
+        _orthogonalize_batch is overridden: its output tensor changes every step)."""
         ns_steps = int(group["ns_steps"])
         recs = [self._prepare(params, shape, group) for shape, params in batches]
         self._front_all(recs, group)
@@ -317,23 +324,165 @@ class NorMuonGNS(torch.optim.Optimizer):
                 self._ortho_class(members, ns_steps)
         self._apply_all(recs, group)
 
+    # ------------------------------------------------- cached launch plans --
+    def invalidate_plan(self) -> None:
+        """Drops the cached launch descriptors (rebuilt on the next step). Needed
+        only after replacing a state tensor object by hand; steps detect new
+        parameters, moved parameter storage, gradients appearing or vanishing,
+        EMA folding and shard changes themselves."""
+        self._plans = {}
+
+    def _build_plan(self, gi, params, group, key):
+        """Every descriptor of one group's step except the gradient pointers:
+        front calls (pointer tables of gradients and momentum buffers), one
+        orthogonaliser call per m-class, finish + apply calls (parameters,
+        remainders, v_row, EMA shadows)."""
+        lib = _lib.load()
+        by_shape = OrderedDict()  # exact-shape buckets in param order (sol_modules.py:380-383)
+        for p in params:
+            by_shape.setdefault(tuple(p.shape), []).append(p)
+        batches = [(shape, ps[i:i + MAX_BATCH]) for shape, ps in by_shape.items()
+                   for i in range(0, len(ps), MAX_BATCH)]
+        recs = [self._prepare(ps, shape, group) for shape, ps in batches]
+        keep, slots = [], {}
+        front = []
+        for (dev, dt), members in self._calls(recs, lambda b: (b["dev"], b["params"][0].dtype)):
+            arr = (_lib.NormuonBatch * len(members))()
+            for i, b in enumerate(members):
+                grads = _lib.ptr_array([None] * b["S"])
+                bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in b["states"]])
+                keep += [grads, bufs]
+                for j, p in enumerate(b["params"]):
+                    slots[id(p)] = (grads, j)
+                ws = b["ws"]
+                arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"], grads=_lib.addr(grads),
+                                           bufs=_lib.addr(bufs), u=ws["u"].data_ptr(),
+                                           partial=ws["partial"].data_ptr(), prescale=ws["prescale"].data_ptr(),
+                                           xscale=ws["xscale"].data_ptr(), flags=ws["flags"].data_ptr(),
+                                           x0_half=int(b["x0"]))
+            front.append((arr, len(members), _lib.dtype_code(dt), _lib.stream_ptr(dev),
+                          any(b["x0"] for b in members)))
+        ortho = []
+        classes = OrderedDict()
+        for b in recs:
+            classes.setdefault((b["dev"], min(b["r"], b["c"])), []).append(b)
+        for (dev, m), members in classes.items():
+            groups = (_lib.OrthoGroup * len(members))()
+            for i, b in enumerate(members):
+                ws = b["ws"]
+                groups[i] = _lib.OrthoGroup(ws["u"].data_ptr(), ws["partial"].data_ptr(), ws["o"].data_ptr(),
+                                            ws["rowsq"].data_ptr(), b["S"], b["r"], b["c"], 0,
+                                            ws["xscale"].data_ptr() if b.get("x0") else None)
+            okey = ("multi",) + tuple((b["S"], b["r"], b["c"]) for b in members)
+            nbytes = lib.b2o_ortho_workspace_bytes_multi(groups, len(members))
+            wsb = self._ortho_ws(dev, okey, nbytes)
+            ortho.append((groups, len(members), wsb, _lib.stream_ptr(dev), m))
+        apply, ema_idx = [], set()
+
+        def akey(b):
+            p0 = b["params"][0]
+            return (b["dev"], p0.dtype, bool(self.bf16_master and p0.dtype == torch.bfloat16))
+
+        for (dev, dt, mt), members in self._calls(recs, akey):
+            arr = (_lib.NormuonBatch * len(members))()
+            for i, b in enumerate(members):
+                ps, states, ws = b["params"], b["states"], b["ws"]
+                pptr = _lib.ptr_array([p.data_ptr() for p in ps])
+                rems = _lib.ptr_array([st["mant_rem"].data_ptr() for st in states]) if mt else None
+                vrows = _lib.ptr_array([st["v_row"].data_ptr() for st in states])
+                emas = None
+                if self._ema is not None:
+                    shadows = [self._ema._lookup(p) for p in ps]
+                    if all(x is not None for x in shadows):
+                        emas = _lib.ptr_array([x.data_ptr() for x in shadows])
+                        ema_idx.update(self._ema._index[id(p)] for p in ps)
+                keep += [pptr, rems, vrows, emas]
+                arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"],
+                                           shape_scale=math.sqrt(max(1.0, b["r"] / b["c"])),
+                                           o=ws["o"].data_ptr(), rowsq=ws["rowsq"].data_ptr(),
+                                           params=_lib.addr(pptr), rems=_lib.addr(rems), emas=_lib.addr(emas),
+                                           vrows=_lib.addr(vrows), scratch=ws["scratch"].data_ptr())
+            apply.append((arr, len(members), _lib.dtype_code(dt), _lib.stream_ptr(dev)))
+        states = [self.state[p] for p in params]
+        return {"key": key, "ema": self._ema, "owned": self._owned, "keep": (keep, params, states, recs),
+                "state_ids": tuple(map(id, states)), "slots": slots, "front": front, "ortho": ortho,
+                "apply": apply, "ema_idx": frozenset(ema_idx)}
+
+    def _run_plan(self, plan, params, group):
+        lib = _lib.load()
+        slots = plan["slots"]
+        for p in params:
+            arr, j = slots[id(p)]
+            arr[j] = p.grad.data_ptr()
+        beta = float(group["momentum"])
+        nesterov = int(bool(group["nesterov"]))
+        gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
+        for arr, n, dtc, stream, x0 in plan["front"]:
+            args = (arr, n, dtc, 1.0 - beta, beta, nesterov, gs)
+            _lib.check(lib.b2o_normuon_front_multi(*args, stream), "normuon_front")
+            if x0:
+                _lib.check(lib.b2o_normuon_prescale(*args, self.norm_eps, self.norm_safety, stream),
+                           "normuon_prescale")
+        ns_steps = int(group["ns_steps"])
+        coeffs, resets, nres = self._table(ns_steps)
+        mode = 0 if self.orthogonalizer == "quintic" else 1
+        ev = self._timing_events
+        for groups, n, wsb, stream, m in plan["ortho"]:
+            if ev is not None:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                n0 = _lib.launch_count()
+            rc = lib.b2o_orthogonalize_multi(groups, n, mode, coeffs, ns_steps, resets, nres, self.norm_eps,
+                                             self.norm_safety, wsb.data_ptr(), wsb.numel(), stream)
+            _lib.check(rc, "orthogonalize_multi")
+            if ev is not None:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                ev.append((e0, e1, m, _lib.launch_count() - n0))
+        beta2 = float(group["beta2"])
+        lr, wd = float(group["lr"]), float(group["weight_decay"])
+        for arr, n, dtc, stream in plan["apply"]:
+            rc = lib.b2o_normuon_apply_multi(arr, n, dtc, -lr, lr * wd, 1.0 - lr * wd, 1 if wd else 0,
+                                             int(bool(self.cautious_wd and wd)), 1.0 - beta2, self._ema_weight,
+                                             stream)
+            _lib.check(rc, "normuon_apply")
+        if self._ema is not None and plan["ema_idx"]:
+            self._ema._folded |= plan["ema_idx"]
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        for group in self.param_groups:
-            by_shape = OrderedDict()  # exact-shape buckets in param order (sol_modules.py:380-383)
+        hooked = self._hook_overridden()
+        owned = self._owned
+        for gi, group in enumerate(self.param_groups):
+            params = []
             for p in group["params"]:
-                if p.grad is None:
+                g = p.grad
+                if g is None or (owned is not None and id(p) not in owned):
                     continue
-                if self._owned is not None and id(p) not in self._owned:
-                    continue
-                by_shape.setdefault(tuple(p.shape), []).append(p)
-            batches = [(shape, params[i:i + MAX_BATCH]) for shape, params in by_shape.items()
-                       for i in range(0, len(params), MAX_BATCH)]
-            if batches:
-                self._step_group(batches, group)
+                if g.dtype != p.dtype or not g.is_contiguous():
+                    raise ValueError("NorMuonGNS needs contiguous params and grads of the param dtype")
+                params.append(p)
+            if not params:
+                continue
+            if hooked:
+                by_shape = OrderedDict()  # exact-shape buckets in param order (sol_modules.py:380-383)
+                for p in params:
+                    by_shape.setdefault(tuple(p.shape), []).append(p)
+                self._step_group([(shape, ps[i:i + MAX_BATCH]) for shape, ps in by_shape.items()
+                                  for i in range(0, len(ps), MAX_BATCH)], group)
+                continue
+            # The launch descriptors depend only on which parameters step, where
+            # their storage and state live, the EMA folding and the shard: cached
+            # across steps; gradient pointers and scalars are filled in each step.
+            key = tuple((id(p), p.data_ptr()) for p in params)
+            plan = self._plans.get(gi)
+            if (plan is None or plan["key"] != key or plan["ema"] is not self._ema or plan["owned"] is not owned
+                    or plan["state_ids"] != tuple(id(self.state.get(p)) for p in params)):
+                plan = self._plans[gi] = self._build_plan(gi, params, group, key)
+            self._run_plan(plan, params, group)
         self._grad_scale = None
         return loss

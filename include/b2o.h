@@ -231,7 +231,9 @@ int b2o_normuon_apply_multi(const b2o_normuon_batch* batches, int nbatches, int 
  * rejected with a negative status and a message, nothing launched. The library
  * allocates nothing: the first call on a device looks up the array's device
  * address (cudaGetSymbolAddress, once per device, with that device current),
- * so make that first call before any stream capture. All calls share the one
+ * so make that first call before any stream capture. The address is cached
+ * for the life of the device's primary context: after a cudaDeviceReset in
+ * the same process, do not call this entry point again. All calls share the one
  * array per device: two calls whose kernels overlap on the GPU (different
  * streams, no ordering between them) race on it. Every scratch value the
  * kernels read is written earlier in the same call, so no clearing is needed.

@@ -16,8 +16,6 @@ import torch
 
 from sol_b200 import _lib
 
-pytestmark = pytest.mark.gpu
-
 
 def _batch(dev, S, r, c, seed):
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -54,6 +52,7 @@ def _call(lib, static, o, rowsq, st, scratch=None, lr=8e-3, wd=0.1, beta2=0.95, 
     _lib.check(rc, "normuon_apply_static" if static else "normuon_apply")
 
 
+@pytest.mark.gpu
 @pytest.mark.parametrize("S,r,c", [(3, 384, 128), (2, 128, 640), (14, 1024, 1024)])
 def test_static_scratch_matches_caller_scratch(S, r, c):
     assert torch.cuda.is_available(), "GPU test run without a CUDA device"
@@ -76,6 +75,7 @@ def test_static_scratch_matches_caller_scratch(S, r, c):
 
 
 def test_static_scratch_rejects_batches_that_do_not_fit():
+    """Host-side size guard only (nothing is launched), so it runs without a GPU too."""
     lib = _lib.load()
     limit = lib.b2o_normuon_apply_static_max_floats()
     assert limit == 1 << 18
