@@ -296,8 +296,9 @@ def engine_arm(args, world, rank, local):
     muon, adamw = build_optimizers(model, orthogonalizer=args.orthogonalizer, coefficients=args.coefficients,
                                    adam_master="bf16_mt", **RECIPE)
     ema = EmaWeights(model, 0.999)
-    sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank,
-                          exchange=args.exchange, push_streams=args.push_streams) if world > 1 else None
+    sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, exchange=args.exchange,
+                          push_streams=args.push_streams, waves=args.waves,
+                          assignment=args.assignment) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     ortho_events = []
     adam_ev = []
@@ -421,7 +422,9 @@ def engine_arm(args, world, rank, local):
                    "l2": "working set > L2 (126 MB); no flush",
                    "parallelism": f"shard{world}" if world > 1 else "single",
                    "exchange": sharded.exchange if sharded is not None else None,
-                   "push_streams": sharded.push_streams if sharded is not None else None},
+                   "push_streams": sharded.push_streams if sharded is not None else None,
+                   "waves": sharded.waves if sharded is not None else None,
+                   "assignment": sharded.assignment if sharded is not None else None},
         "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
                       "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
         "sharded_phases_ms": shard_phases or None,
@@ -493,7 +496,7 @@ def sharded_parity(args, cfg, world, rank, dev, steps=3):
     muon, adamw = build_optimizers(model, **kw)
     ema = EmaWeights(model, 0.999)
     sh = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, exchange=args.exchange,
-                     push_streams=args.push_streams)
+                     push_streams=args.push_streams, waves=args.waves, assignment=args.assignment)
     ref = synth.SyntheticLM(cfg, device=dev, seed=0)
     rmuon, radamw = build_optimizers(ref, **kw)
     rema = EmaWeights(ref, 0.999)
@@ -706,6 +709,8 @@ def main():
     ap.add_argument("--exchange", default="auto", choices=["auto", "ce", "hybrid", "nccl"],
                     help="N>1: copy-engine pushes over CUDA IPC mappings, NCCL all-gathers, or both")
     ap.add_argument("--push-streams", type=int, default=1, help="N>1: streams the copy-engine pushes use")
+    ap.add_argument("--waves", type=int, default=1, help="N>1: NorMuon waves per rank (exchange overlaps compute)")
+    ap.add_argument("--assignment", default="lpt", choices=["lpt", "runs"], help="N>1: matrix-to-rank assignment")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="N=1: skip the configs[2]/[3] micro-benchmarks")

@@ -262,10 +262,21 @@ def ipc_close(base: int) -> None:
     check(load().b2o_ipc_close(base), "ipc_close")
 
 
-def copy_async(copies, stream: int) -> None:
-    """Enqueues device-to-device copies [(dst_ptr, src_ptr, nbytes), ...] on stream."""
+def copy_args(copies):
+    """ctypes arguments of b2o_copy_async for [(dst_ptr, src_ptr, nbytes), ...]."""
     n = len(copies)
     dst = ptr_array([d for d, _, _ in copies])
     src = ptr_array([s for _, s, _ in copies])
     nb = (c_int64 * max(1, n))(*[b for _, _, b in copies])
+    return dst, src, nb, n
+
+
+def copy_async_args(args, stream: int) -> None:
+    """Enqueues the copies prepared by copy_args on stream."""
+    dst, src, nb, n = args
     check(load().b2o_copy_async(dst, src, nb, n, stream), "copy_async")
+
+
+def copy_async(copies, stream: int) -> None:
+    """Enqueues device-to-device copies [(dst_ptr, src_ptr, nbytes), ...] on stream."""
+    copy_async_args(copy_args(copies), stream)

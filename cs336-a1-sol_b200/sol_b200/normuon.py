@@ -80,7 +80,7 @@ class NorMuonGNS(torch.optim.Optimizer):
         # orthogonaliser call (benchmark phase timing); None = off
         self._timing_events = None
         self._grad_scale = None    # device fp32 clip coefficient for the next step (clip_grad_norm_ defer_to)
-        self._plans = {}           # param-group index -> cached launch descriptors (see step)
+        self._plans = {}           # (param-group index, owned set) -> cached launch descriptors (see step)
         register_optimizer(self)
 
     # ------------------------------------------------------------------ hooks
@@ -479,10 +479,11 @@ class NorMuonGNS(torch.optim.Optimizer):
             # their storage and state live, the EMA folding and the shard: cached
             # across steps; gradient pointers and scalars are filled in each step.
             key = tuple((id(p), p.data_ptr()) for p in params)
-            plan = self._plans.get(gi)
+            pkey = (gi, id(owned))  # a sharded step alternates between its waves' owned sets
+            plan = self._plans.get(pkey)
             if (plan is None or plan["key"] != key or plan["ema"] is not self._ema or plan["owned"] is not owned
                     or plan["state_ids"] != tuple(id(self.state.get(p)) for p in params)):
-                plan = self._plans[gi] = self._build_plan(gi, params, group, key)
+                plan = self._plans[pkey] = self._build_plan(gi, params, group, key)
             self._run_plan(plan, params, group)
         self._grad_scale = None
         return loss

@@ -4,9 +4,9 @@ The reference is single-GPU (no torch.distributed call sites); this is the
 north-star's partitioned step. Placement never changes per-matrix arithmetic,
 so every rank's result is bit-identical to the single-GPU engine.
 
-  * NorMuon: whole matrices are assigned to ranks (greedy longest-processing-time
-    on the Gram Newton-Schulz FLOP count); each rank batches its own matrices by
-    shape. The NorMuon parameters are re-pointed into one flat bf16 arena laid
+  * NorMuon: whole matrices are assigned to ranks in contiguous runs of a
+    shape-sorted list, cut to balance a model of each rank's launch rounds
+    (assign_matrices); each rank batches its own matrices by shape. The NorMuon parameters are re-pointed into one flat bf16 arena laid
     out rank by rank, so the exchange is a single in-place all-gather.
   * AdamW: tables whose row count divides by the world size are split by rows
     (each rank updates its rows; in-place all-gather per table); the small
@@ -36,33 +36,148 @@ from . import _lib
 
 
 def gram_cost(shape) -> float:
+    """Orthogonaliser FLOPs of one matrix as the engine runs it: two Gram
+    products X X^T and two Q X products (6 m^2 n, symmetric outputs at half)
+    and fourteen symmetric m x m products (14 m^3)."""
     r, c = shape[-2], shape[-1]
     m, n = min(r, c), max(r, c)
-    return 6.0 * m * m * n + 20.0 * m ** 3
+    return 6.0 * m * m * n + 14.0 * m ** 3
 
 
-def assign_matrices(shapes, world):
-    """Greedy LPT: returns owner rank per matrix (ties broken by rank index)."""
-    order = sorted(range(len(shapes)), key=lambda i: (-gram_cost(shapes[i]), i))
+# Cost model of one rank's NorMuon share, in microseconds on one B200: GEMM
+# launches run in rounds of 256 x 256 tiles over 74 CTA pairs (a launch with
+# 75 tiles costs two rounds), a round costs K x 5.9 ns (a pair tile at the
+# measured 1642 TFLOP/s), every launch a few microseconds of fill and drain;
+# the front and apply passes stream 26 bytes per element at copy bandwidth.
+_PAIRS = 74
+_ROUND_NS_PER_K = 7.7
+_LAUNCH_US = 4.0
+_STREAM_B_PER_ELEM = 26.0
+_HBM_B_PER_US = 6.5e6
+
+
+def _tiles(a: int) -> int:
+    return -(-a // 256)
+
+
+def rank_cost_us(shapes) -> float:
+    """Modelled time of the NorMuon step of one rank owning these matrices."""
+    groups, classes = {}, {}
+    for sh in shapes:
+        groups[tuple(sh)] = groups.get(tuple(sh), 0) + 1
+    us = 0.0
+    for (r, c), s in groups.items():
+        m, n = min(r, c), max(r, c)
+        us += s * r * c * _STREAM_B_PER_ELEM / _HBM_B_PER_US
+        if m <= 32:
+            us += _LAUNCH_US
+            continue
+        classes[m] = classes.get(m, 0) + s
+        sym = _tiles(m) * (_tiles(m) + 1) // 2
+        syrk = -(-s * sym // _PAIRS) * n * _ROUND_NS_PER_K / 1e3
+        qx = -(-s * _tiles(r) * _tiles(c) // _PAIRS) * m * _ROUND_NS_PER_K / 1e3
+        us += 2 * (syrk + qx) + 4 * _LAUNCH_US
+    for m, s in classes.items():
+        sym = _tiles(m) * (_tiles(m) + 1) // 2
+        us += 14 * (-(-s * sym // _PAIRS) * m * _ROUND_NS_PER_K / 1e3 + _LAUNCH_US)
+    return us
+
+
+def _shape_order_key(shape):
+    r, c = shape[-2], shape[-1]
+    return (min(r, c) <= 32, -max(r, c), -min(r, c), 0 if r > c else 1, (r, c))
+
+
+def _contiguous_runs(shapes, parts):
+    """Cuts `shapes` (in the given order) into at most `parts` contiguous runs
+    minimising the largest rank_cost_us of a run (dynamic programming over cut
+    points, ties towards the earlier cut). Returns [(start, end)] and costs."""
+    n = len(shapes)
+    cost = [[0.0] * (n + 1) for _ in range(n + 1)]
+    for i in range(n):
+        for j in range(i + 1, n + 1):
+            cost[i][j] = rank_cost_us(shapes[i:j])
+    inf = float("inf")
+    k_max = max(1, min(parts, n))
+    best = [[inf] * (n + 1) for _ in range(k_max + 1)]
+    cut = [[0] * (n + 1) for _ in range(k_max + 1)]
+    best[0][0] = 0.0
+    for k in range(1, k_max + 1):
+        for j in range(k, n + 1):
+            for i in range(k - 1, j):
+                v = max(best[k - 1][i], cost[i][j])
+                if v < best[k][j] - 1e-9:
+                    best[k][j], cut[k][j] = v, i
+    bounds, j = [], n
+    for k in range(k_max, 0, -1):
+        i = cut[k][j]
+        bounds.append((i, j))
+        j = i
+    bounds.reverse()
+    return bounds, [cost[i][j] for i, j in bounds]
+
+
+def assign_matrices(shapes, world, method: str = "lpt"):
+    """Owner rank per matrix and each rank's load.
+
+    "lpt": greedy longest-processing-time on gram_cost (load in FLOPs).
+    "runs": matrices sorted by shape (largest n first, tall before wide, the
+    one-CTA small matrices last) and cut into `world` contiguous runs that
+    minimise the largest modelled rank cost (load in modelled microseconds);
+    each rank then holds one or two shape batches, so its GEMM launches have
+    as many tiles as its share allows. Both are deterministic, so every rank
+    computes the same assignment."""
+    n = len(shapes)
+    if n == 0:
+        return [], [0.0] * world
+    if method == "lpt":
+        order = sorted(range(n), key=lambda i: (-gram_cost(shapes[i]), i))
+        load = [0.0] * world
+        owner = [0] * n
+        for i in order:
+            k = min(range(world), key=lambda r: (load[r], r))
+            owner[i] = k
+            load[k] += gram_cost(shapes[i])
+        return owner, load
+    if method != "runs":
+        raise ValueError("assignment must be 'lpt' or 'runs'")
+    order = sorted(range(n), key=lambda i: (_shape_order_key(shapes[i]), i))
+    bounds, costs = _contiguous_runs([tuple(shapes[i]) for i in order], world)
+    owner = [0] * n
     load = [0.0] * world
-    owner = [0] * len(shapes)
-    for i in order:
-        k = min(range(world), key=lambda r: (load[r], r))
-        owner[i] = k
-        load[k] += gram_cost(shapes[i])
+    for rank, ((i, j), c) in enumerate(zip(bounds, costs)):
+        for pos in range(i, j):
+            owner[order[pos]] = rank
+        load[rank] = c
     return owner, load
+
+
+def split_waves(shapes, waves: int):
+    """Splits one rank's matrices (indices into `shapes`) into `waves` runs of
+    similar modelled cost, each run one or two shape batches."""
+    n = len(shapes)
+    if waves <= 1 or n <= 1:
+        return [list(range(n))]
+    order = sorted(range(n), key=lambda i: (_shape_order_key(shapes[i]), i))
+    bounds, _ = _contiguous_runs([tuple(shapes[i]) for i in order], waves)
+    return [sorted(order[i:j]) for i, j in bounds]
 
 
 class ShardedStep:
     def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024,
-                 exchange: str = "auto", push_streams: int = 1):
+                 exchange: str = "auto", push_streams: int = 1, waves: int = 1, assignment: str = "lpt"):
         """exchange: "ce" (copy-engine pushes of the tables and the arena),
         "hybrid" (copy-engine pushes of the tables, overlapped with NorMuon;
         NCCL all-gather of the arena), "nccl" (all-gathers only) or "auto".
         Copy-engine modes fall back to NCCL where a rank cannot export its
         buffers ("auto") or raise. push_streams: streams the pushes are spread
         over; peers are visited in ring order rank+1, rank+2, ... so with one
-        stream every rank sends to one peer at a time."""
+        stream every rank sends to one peer at a time.
+        waves: each rank steps its NorMuon matrices in this many waves and
+        starts exchanging a wave's weights as soon as that wave is applied, so
+        the exchange overlaps the next wave's compute (the arena is laid out
+        wave by wave, each wave rank by rank).
+        assignment: "lpt" or "runs" (see assign_matrices)."""
         if exchange not in ("auto", "ce", "hybrid", "nccl"):
             raise ValueError("exchange must be 'auto', 'ce', 'hybrid' or 'nccl'")
         required = exchange != "auto"
@@ -76,28 +191,48 @@ class ShardedStep:
         self.push_streams = max(1, min(int(push_streams), max(1, world - 1)))
         self.muon, self.adamw, self.ema = muon, adamw, ema
         mparams = [p for g in muon.param_groups for p in g["params"]]
-        owner, self.load = assign_matrices([tuple(p.shape) for p in mparams], world)
+        owner, self.load = assign_matrices([tuple(p.shape) for p in mparams], world, assignment)
+        self.assignment = assignment
         self.owner = {id(p): k for p, k in zip(mparams, owner)}
         muon._owned = {id(p) for p, k in zip(mparams, owner) if k == rank}
-        # flat arena laid out rank by rank
+        self.owned_all = muon._owned
+        # every rank's matrices split into the same number of waves
+        self.waves = max(1, int(waves))
+        per_rank = [[p for p, k in zip(mparams, owner) if k == r] for r in range(world)]
+        wave_of = {}
+        for r, ps in enumerate(per_rank):
+            for w, idx in enumerate(split_waves([tuple(p.shape) for p in ps], self.waves)):
+                for i in idx:
+                    wave_of[id(ps[i])] = w
+        self.wave_owned = [{id(p) for p in per_rank[rank] if wave_of[id(p)] == w} for w in range(self.waves)]
+        # flat arena: wave by wave, each wave's region rank by rank (equal chunks
+        # per wave, so each wave is one all-gather)
         dt = mparams[0].dtype if mparams else torch.bfloat16
         dev = mparams[0].device if mparams else torch.device("cuda")
-        per_rank = [[p for p, k in zip(mparams, owner) if k == r] for r in range(world)]
         align = 64
-        sizes = [sum((p.numel() + align - 1) // align * align for p in ps) for ps in per_rank]
-        self.chunk = max(sizes) if sizes else 0
-        self.arena_used = sizes  # elements of each rank's chunk that hold parameters
-        self.arena = torch.empty(self.chunk * world, dtype=dt, device=dev)
-        for r, ps in enumerate(per_rank):
-            off = r * self.chunk
-            for p in ps:
-                if p.dtype != dt:
-                    raise ValueError("NorMuon parameters must share one dtype for the gather arena")
-                n = p.numel()
-                view = self.arena[off:off + n].view_as(p)
-                view.copy_(p.data)
-                p.data = view
-                off += (n + align - 1) // align * align
+        rnd = lambda n: (n + align - 1) // align * align  # noqa: E731
+        self.arena_waves = []  # (base element, chunk elements, used elements per rank)
+        base = 0
+        for w in range(self.waves):
+            used = [sum(rnd(p.numel()) for p in ps if wave_of[id(p)] == w) for ps in per_rank]
+            chunk = max(used) if used else 0
+            self.arena_waves.append((base, chunk, used))
+            base += chunk * world
+        self.arena = torch.empty(base, dtype=dt, device=dev)
+        for w, (wbase, chunk, _) in enumerate(self.arena_waves):
+            for r, ps in enumerate(per_rank):
+                off = wbase + r * chunk
+                for p in ps:
+                    if wave_of[id(p)] != w:
+                        continue
+                    if p.dtype != dt:
+                        raise ValueError("NorMuon parameters must share one dtype for the gather arena")
+                    n = p.numel()
+                    view = self.arena[off:off + n].view_as(p)
+                    view.copy_(p.data)
+                    p.data = view
+                    off += rnd(n)
+        self.chunk = sum(c for _, c, _ in self.arena_waves)  # elements per rank over all waves
         # AdamW row shards
         self.row_sharded = []
         slices = {}
@@ -133,12 +268,15 @@ class ShardedStep:
         """Tensors exchanged between ranks: the NorMuon arena, then each row-sharded table."""
         return [self.arena] + [p.data for p in self.row_sharded]
 
+    def arena_regions(self, rank: int):
+        """(wave, byte offset, bytes) of the arena parts `rank` updates."""
+        es = self.arena.element_size()
+        return [(w, (base + rank * chunk) * es, used[rank] * es)
+                for w, (base, chunk, used) in enumerate(self.arena_waves) if used[rank]]
+
     def owned_regions(self, rank: int):
         """(buffer index, byte offset, bytes) of what `rank` updates in each exchanged buffer."""
-        es = self.arena.element_size()
-        regions = []
-        if self.chunk and self.arena_used[rank]:
-            regions.append((0, rank * self.chunk * es, self.arena_used[rank] * es))
+        regions = [(0, off, nbytes) for _, off, nbytes in self.arena_regions(rank)]
         for i, p in enumerate(self.row_sharded):
             per = p.numel() // self.world
             regions.append((1 + i, rank * per * p.element_size(), per * p.element_size()))
@@ -179,13 +317,19 @@ class ShardedStep:
             self._streams = [torch.cuda.Stream(dev) for _ in range(self.push_streams)]
         local = [b.data_ptr() for b in bufs]
         # per stream, the copies in ring order of the peers
-        plans = {"tables": [[] for _ in self._streams], "arena": [[] for _ in self._streams]}
+        plans = {"tables": [[] for _ in self._streams]}
+        for w in range(self.waves):
+            plans[f"arena{w}"] = [[] for _ in self._streams]
         for d in range(1, self.world):
             q = (self.rank + d) % self.world
+            st = (d - 1) % self.push_streams
+            for w, off, nbytes in self.arena_regions(self.rank):
+                plans[f"arena{w}"][st].append((peer_ptrs[q][0] + off, local[0] + off, nbytes))
             for k, off, nbytes in self.owned_regions(self.rank):
-                which = "arena" if k == 0 else "tables"
-                plans[which][(d - 1) % self.push_streams].append((peer_ptrs[q][k] + off, local[k] + off, nbytes))
-        self._plans = plans
+                if k > 0:
+                    plans["tables"][st].append((peer_ptrs[q][k] + off, local[k] + off, nbytes))
+        # ctypes argument arrays built once: the pushes reuse them every step
+        self._plans = {k: [_lib.copy_args(c) if c else None for c in per_stream] for k, per_stream in plans.items()}
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
         self.exchange = self._requested
 
@@ -193,10 +337,10 @@ class ShardedStep:
         cur = torch.cuda.current_stream()
         ev = torch.cuda.Event()
         ev.record(cur)
-        for st, copies in zip(self._streams, self._plans[which]):
-            if copies:
+        for st, args in zip(self._streams, self._plans[which]):
+            if args is not None:
                 st.wait_event(ev)
-                _lib.copy_async(copies, st.cuda_stream)
+                _lib.copy_async_args(args, st.cuda_stream)
 
     def _join_pushes(self):
         cur = torch.cuda.current_stream()
@@ -227,11 +371,17 @@ class ShardedStep:
                 works.append(w)
         return works
 
-    def _gather_arena(self, async_op=False):
-        if not self.chunk:
+    def _gather_arena_wave(self, w, async_op=False):
+        base, chunk, _ = self.arena_waves[w]
+        if not chunk:
             return None
-        mine = self.arena[self.rank * self.chunk:(self.rank + 1) * self.chunk]
-        return dist.all_gather_into_tensor(self.arena, mine, group=self.group, async_op=async_op)
+        region = self.arena[base:base + chunk * self.world]
+        mine = region[self.rank * chunk:(self.rank + 1) * chunk]
+        return dist.all_gather_into_tensor(region, mine, group=self.group, async_op=async_op)
+
+    def _gather_arena(self, async_op=False):
+        works = [self._gather_arena_wave(w, async_op) for w in range(self.waves)]
+        return [x for x in works if x is not None]
 
     @torch.no_grad()
     def gather(self):
@@ -243,9 +393,12 @@ class ShardedStep:
 
     @torch.no_grad()
     def step(self, mark=None, before=None):
-        """One sharded optimizer step: AdamW first, so the all-gathers of the
-        vocabulary tables run on NCCL's stream while NorMuon computes; then
-        NorMuon, the EMA update and the all-gather of the NorMuon arena.
+        """One sharded optimizer step: AdamW first, so the vocabulary tables
+        cross NVLink (copy-engine pushes, or NCCL all-gathers on NCCL's stream)
+        while NorMuon computes; then NorMuon wave by wave, each wave's arena
+        region exchanged as soon as the wave is applied (copy-engine pushes or
+        an NCCL all-gather on NCCL's stream) while the next wave computes; the
+        EMA update; the completion of every exchange.
         Same results as muon.step(); adamw.step(); ema.update(); gather().
         ``mark(name)``, when given, is called after each phase is enqueued
         (phase timing with events on the current stream); ``before(name)`` is
@@ -263,23 +416,37 @@ class ShardedStep:
         elif self.world > 1:
             works = self._gather_tables(async_op=True)
         before("normuon")
-        self.muon.step()
+        arena_works = []
+        try:
+            for w in range(self.waves):
+                self.muon._owned = self.wave_owned[w]
+                self.muon.step()
+                if self.world > 1:
+                    if self.exchange == "ce":
+                        self._push(f"arena{w}")
+                    elif w < self.waves - 1:
+                        x = self._gather_arena_wave(w, async_op=True)
+                        if x is not None:
+                            arena_works.append(x)
+        finally:
+            self.muon._owned = self.owned_all
         mark("normuon")
         if self.ema is not None:
             self.ema.update()
         if self.exchange == "ce":
-            self._push("arena")
             self._join_pushes()
             # every rank enters this collective only after its own pushes
             # landed, so its completion means every rank's pushes did
             dist.all_reduce(self._flag, group=self.group)
         elif self.world > 1:
             if push_tables:
-                self._join_pushes()  # the arena all-gather is then also the pushes' barrier
-            self._gather_arena()
+                self._join_pushes()  # the last all-gather is then also the pushes' barrier
+            self._gather_arena_wave(self.waves - 1)
+            for x in arena_works:
+                x.wait()
         mark("arena_gather")
-        for w in works:
-            w.wait()
+        for x in works:
+            x.wait()
         mark("table_wait")
 
     @torch.no_grad()
@@ -311,13 +478,23 @@ class ShardedStep:
                 offs.append(off)
                 if p.grad is not None:
                     self._grad_arena[off:off + p.numel()].copy_(p.grad.view(-1))
-            dist.reduce_scatter_tensor(self._grad_out, self._grad_arena, group=self.group)
+            # one reduce-scatter per wave region ([rank 0 | rank 1 | ...] each)
+            out_base, ob = [], 0
+            for base, chunk, _ in self.arena_waves:
+                out_base.append(ob)
+                if chunk:
+                    dist.reduce_scatter_tensor(self._grad_out[ob:ob + chunk],
+                                               self._grad_arena[base:base + chunk * self.world], group=self.group)
+                ob += chunk
             if scale is not None:
                 self._grad_out.mul_(scale)
-            lo = self.rank * self.chunk
             for p, off in zip(mparams, offs):
                 if self.owner[id(p)] == self.rank and p.grad is not None:
-                    p.grad.view(-1).copy_(self._grad_out[off - lo:off - lo + p.numel()])
+                    for (base, chunk, _), o in zip(self.arena_waves, out_base):
+                        lo = base + self.rank * chunk
+                        if lo <= off < lo + chunk:
+                            p.grad.view(-1).copy_(self._grad_out[o + off - lo:o + off - lo + p.numel()])
+                            break
         for p in self.row_sharded:
             if p.grad is None:
                 continue

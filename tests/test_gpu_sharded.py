@@ -27,7 +27,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, exchange, q, dp=False):
+def _worker(rank, world, port, exchange, q, dp=False, waves=1, assignment="lpt"):
     import torch.distributed as dist
 
     from sol_b200 import EmaWeights, build_optimizers, synth
@@ -46,7 +46,7 @@ def _worker(rank, world, port, exchange, q, dp=False):
         muon, adamw = build_optimizers(model, adam_master="bf16_mt", **KW)
         ema = EmaWeights(model, 0.999)
         sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16,
-                              exchange=exchange)
+                              exchange=exchange, waves=waves, assignment=assignment)
         ref = synth.SyntheticLM(cfg, device=dev, seed=0)
         rmuon, radamw = build_optimizers(ref, adam_master="bf16_mt", **KW)
         rema = EmaWeights(ref, 0.999)
@@ -100,17 +100,21 @@ def _worker(rank, world, port, exchange, q, dp=False):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange,dp", [("ce", False), ("hybrid", False), ("nccl", False), ("auto", True)])
-def test_sharded_step_bit_identical_to_single_gpu(exchange, dp):
+@pytest.mark.parametrize("exchange,dp,waves,assignment", [
+    ("ce", False, 1, "lpt"), ("hybrid", False, 1, "lpt"), ("nccl", False, 1, "lpt"), ("auto", True, 1, "lpt"),
+    ("ce", False, 2, "runs"), ("hybrid", False, 2, "lpt"), ("nccl", True, 2, "runs")])
+def test_sharded_step_bit_identical_to_single_gpu(exchange, dp, waves, assignment):
     """dp: each rank steps on its own gradients after reduce_gradients; the
-    single-GPU reference steps on their mean."""
+    single-GPU reference steps on their mean. waves > 1: each wave's weights
+    are exchanged while the next wave computes."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q, dp)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q, dp, waves, assignment))
+             for r in range(world)]
     for p in procs:
         p.start()
     out = {}

@@ -39,6 +39,13 @@ def test_partition_is_balanced_and_deterministic(world):
     total = sum(gram_cost(s) for s in shapes)
     biggest = max(gram_cost(s) for s in shapes)
     assert max(load) <= total / world + biggest  # LPT bound
+    owner2, load2 = assign_matrices(shapes, world, "runs")
+    assert owner2 == assign_matrices(shapes, world, "runs")[0]
+    assert sorted(set(owner2)) == list(range(world))
+    # shape runs: every rank holds at most three GEMM-path shapes (the 8 x 1024
+    # gates run in their own one-CTA kernel)
+    for r in range(world):
+        assert len({shapes[i] for i in range(len(shapes)) if owner2[i] == r and min(shapes[i]) > 32}) <= 3
 
 
 def _expected(name, shape, dtype):
@@ -46,7 +53,7 @@ def _expected(name, shape, dtype):
     return torch.randn(shape, generator=g).to(dtype)
 
 
-def _worker(rank, world, port, mode, q):
+def _worker(rank, world, port, mode, q, waves=1, assignment="lpt"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:
@@ -54,7 +61,8 @@ def _worker(rank, world, port, mode, q):
         model = synth.SyntheticLM(synth.MICRO, seed=0)
         muon, adamw = build_optimizers(model, **KW)
         ema = EmaWeights(model, 0.999)
-        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16)
+        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16, waves=waves,
+                              assignment=assignment)
         named = list(model.named_parameters())
         # "step": each rank writes the final values of what it owns
         with torch.no_grad():
@@ -94,11 +102,11 @@ def _worker(rank, world, port, mode, q):
             dist.destroy_process_group()
 
 
-def _run(world, mode):
+def _run(world, mode, waves=1, assignment="lpt"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q, waves, assignment)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -112,9 +120,10 @@ def _run(world, mode):
     return out
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gather_reassembles_every_parameter(world):
-    out = _run(world, "ok")
+@pytest.mark.parametrize("world,waves,assignment", [(2, 1, "lpt"), (3, 1, "lpt"), (2, 2, "runs"), (3, 3, "lpt")])
+def test_gather_reassembles_every_parameter(world, waves, assignment):
+    """Wave-major arena (waves > 1) and shape-run assignment included."""
+    out = _run(world, "ok", waves, assignment)
     assert sorted(out) == list(range(world))
     for r, v in out.items():
         assert v["bad"] == [], (r, v["bad"])
@@ -130,7 +139,7 @@ def test_rank_leaving_is_detected_not_hung():
     assert isinstance(out[0], str) and out[0].startswith("error"), out[0]
 
 
-def _reduce_worker(rank, world, port, average, q):
+def _reduce_worker(rank, world, port, average, q, waves=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:
@@ -138,7 +147,7 @@ def _reduce_worker(rank, world, port, average, q):
         model = synth.SyntheticLM(synth.MICRO, seed=0)
         muon, adamw = build_optimizers(model, **KW)
         ema = EmaWeights(model, 0.999)
-        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16)
+        sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16, waves=waves)
         named = list(model.named_parameters())
         with torch.no_grad():
             for n, p in named:
@@ -171,14 +180,14 @@ def _reduce_worker(rank, world, port, average, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,average", [(2, False), (2, True), (3, True)])
-def test_reduce_gradients_sums_what_each_rank_reads(world, average):
+@pytest.mark.parametrize("world,average,waves", [(2, False, 1), (2, True, 1), (3, True, 1), (3, True, 2)])
+def test_reduce_gradients_sums_what_each_rank_reads(world, average, waves):
     """Each rank holds its own gradients; after reduce_gradients every rank
     holds the sum (or mean) over ranks of the gradients its step reads."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, average, q)) for r in range(world)]
+    procs = [ctx.Process(target=_reduce_worker, args=(r, world, port, average, q, waves)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -198,16 +207,18 @@ def test_reduce_gradients_sums_what_each_rank_reads(world, average):
         assert out[r]["worst_ulps"] <= limit, out[r]
 
 
-@pytest.mark.parametrize("world", [2, 3, 4, 8])
-def test_owned_regions_are_disjoint_and_cover_every_update(world):
+@pytest.mark.parametrize("world,waves,assignment", [(2, 1, "lpt"), (3, 1, "lpt"), (4, 1, "lpt"), (8, 1, "lpt"),
+                                                    (2, 2, "runs"), (4, 2, "runs"), (8, 3, "lpt")])
+def test_owned_regions_are_disjoint_and_cover_every_update(world, waves, assignment):
     """The regions each rank pushes (sharded step) tile every NorMuon matrix and
-    every row-sharded table exactly once."""
+    every row-sharded table exactly once; each wave's owned set is exactly the
+    rank's matrices in that wave's arena region."""
     steps = []
     for rank in range(world):
         model = synth.SyntheticLM(synth.MICRO, seed=0)
         muon, adamw = build_optimizers(model, **KW)
         steps.append(ShardedStep(model, muon, adamw, None, world=world, rank=rank, min_rows_shard=16,
-                                 exchange="nccl"))
+                                 exchange="nccl", waves=waves, assignment=assignment))
     ref = steps[0]
     bufs = ref.buffers()
     covered = [torch.zeros(b.numel() * b.element_size(), dtype=torch.int32) for b in bufs]
@@ -224,3 +235,14 @@ def test_owned_regions_are_disjoint_and_cover_every_update(world):
         assert int(covered[0][off:off + p.numel() * es].min()) == 1
     for k in range(1, len(bufs)):
         assert int(covered[k].min()) == 1
+    for st in steps:
+        assert set().union(*st.wave_owned) == st.owned_all
+        assert sum(len(w) for w in st.wave_owned) == len(st.owned_all)
+        mparams = {id(p): p for g in st.muon.param_groups for p in g["params"]}
+        b0, es0 = st.arena.data_ptr(), st.arena.element_size()
+        for w, ids in enumerate(st.wave_owned):
+            wbase, chunk, _ = st.arena_waves[w]
+            lo = (wbase + st.rank * chunk) * es0
+            for i in ids:
+                off = mparams[i].data.data_ptr() - b0
+                assert lo <= off and off + mparams[i].numel() * es0 <= lo + chunk * es0
