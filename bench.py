@@ -43,7 +43,7 @@ MOM_WARMUP = 300
 # averaged over the 30 launches of one L14 step, from a one-pass ncu capture
 # of this benchmark's default configuration on one GPU (not measured by the
 # run that prints it; reported for that configuration only).
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.169e8
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 2.163e8
 
 
 def peaks():
@@ -131,7 +131,8 @@ class ClockSampler:
             self.nvml.nvmlShutdown()
         except Exception:  # noqa: BLE001
             pass
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+        low = sorted(sm)[len(sm) // 10] if sm else None
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_mhz_p10": low, "sm_max_mhz": self.max_mhz,
                 "reasons": reasons, "samples": len(sm), "window": window, "source": "NVML"}
 
 
@@ -369,11 +370,15 @@ def engine_arm(args, world, rank, local):
     # the m > 32 classes, whose launches are all tcgen05 GEMMs in the default
     # Gram mode (the m <= 32 gates run in one CUDA-core kernel of their own).
     torch.cuda.synchronize()
+    gsampler = ClockSampler(local)  # clocks of this second run, where the GEMM figure comes from
+    gsampler.start()
+    gsampler.mark()
     muon._timing_events = ortho_events
     for k in range(args.steps):
         one_step(args.warmup + args.steps + k, record=True)
     torch.cuda.synchronize()
     muon._timing_events = None
+    gclocks = gsampler.stop()
     err = _lib.device_error()
     if err:
         raise RuntimeError(f"device error word {err}")
@@ -381,6 +386,9 @@ def engine_arm(args, world, rank, local):
     ms = max_over_ranks(ms_local, world, dev)
     ortho_ms = sum(a.elapsed_time(b) for a, b, _, _ in ortho_events) / args.steps
     gemm_ms = sum(a.elapsed_time(b) for a, b, m, _ in ortho_events if m > 32) / args.steps
+    per_step = [a.elapsed_time(b) for a, b, m, _ in ortho_events if m > 32]
+    per_class = max(1, len(per_step) // max(1, args.steps))
+    per_step = [sum(per_step[i:i + per_class]) for i in range(0, len(per_step), per_class)]
     gemm_n = sum(n for _, _, m, n in ortho_events if m > 32) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in adam_ev) / args.steps
     shard_phases = {}
@@ -397,12 +405,17 @@ def engine_arm(args, world, rank, local):
     # outputs at half) over its device time in the step. Denominator: the burst
     # bf16 peak when the SM clock held its maximum through the timed region,
     # the sustained (power-capped) one when the clock samples show it lowered.
-    sm, smax = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
-    at_max = bool(sm and smax and sm >= 0.97 * smax)
+    # the peak follows the clocks of the run the GEMM figure comes from: the
+    # burst figure when neither its clock median nor its power-cap flags show
+    # the GPU below its maximum clock, else the sustained (power-capped) one
+    sm, smax = gclocks.get("sm_mhz"), gclocks.get("sm_max_mhz")
+    capped = "sw_power_cap" in (gclocks.get("reasons") or [])
+    at_max = bool(sm and smax and sm >= 0.97 * smax) and not capped
     peak_tf = peak_burst if at_max or not sm else peak_sus
-    peak_label = (f"{peak_kind} bf16 burst (SM clock median {sm} of max {smax} MHz in the timed region)"
-                  if peak_tf == peak_burst else
-                  f"{peak_kind} bf16 sustained (SM clock median {sm} of max {smax} MHz: power-capped)")
+    peak_label = (f"{peak_kind} bf16 burst (SM clock median {sm} of max {smax} MHz in the GEMM-timing run, no "
+                  "power cap seen)" if peak_tf == peak_burst else
+                  f"{peak_kind} bf16 sustained (SM clock median {sm} of max {smax} MHz in the GEMM-timing run, "
+                  f"power cap {'seen' if capped else 'not seen'})")
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     # AdamW+EMA streaming bytes: p 2+2, rem 2+2, g 2, m 4+4, v 4+4, fp32 EMA 4+4 = 34 B/elem
     adam_elems = sum(p.numel() for g in adamw.param_groups for p in g["params"])
@@ -442,7 +455,9 @@ def engine_arm(args, world, rank, local):
                                "tensor-core classes (30 GEMM launches each, nothing else), second timed run",
                      "peak_kind": peak_label,
                      "frac_of_burst_peak": (achieved / peak_burst) if achieved else None,
-                     "frac_of_sustained_peak": (achieved / peak_sus) if achieved else None},
+                     "frac_of_sustained_peak": (achieved / peak_sus) if achieved else None,
+                     "gemm_ms_first_last_min": [per_step[0], per_step[-1], min(per_step)] if per_step else None,
+                     "clocks": gclocks},
         "orthogonalizer": {"ms_per_step": ortho_ms, "flops_per_step": flops,
                            "tflops": flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None},
         "host_enqueue_ms_per_step": host_t * 1e3 / args.steps,

@@ -300,7 +300,10 @@ def test_full_step_with_ema_matches_reference(cuda):
             assert_f32_ulps(ema.shadow[i], ref.shadow[i], ulps=2, what=f"ema {n}")
     err = (num / den) ** 0.5
     print(f"full step: NorMuon cumulative update rel. Frobenius error after 6 steps = {err:.2e}")
-    assert err < 1.5e-2
+    # quintic mode restates the reference's bf16 iteration rounding for rounding;
+    # against the reference run with torch on the same GPU only the fp32
+    # accumulation order inside the GEMMs differs (measured 9.2e-5)
+    assert err < 1e-3
 
 
 def test_ema_folded_equals_standalone(cuda):
