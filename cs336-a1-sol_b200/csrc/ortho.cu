@@ -39,6 +39,86 @@ static inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * 
 
 constexpr int kPool = 6;
 
+// ---------------------------------------------------------------------------
+// Per-shape-group launches of one call (the Gram products X X^T, the restart
+// Q X0 and the final Q X) are independent across groups; a group with few
+// matrices fills only part of the 74 CTA pairs, so the groups of one phase
+// run on forked streams and share the GPU. Each device keeps a few streams
+// for this, created on first use; the phase forks from the caller's stream
+// with an event and joins back before the next class-wide launch, so the
+// caller's stream order is unchanged and results are identical.
+constexpr int kLanes = 4;
+struct LanePool {
+  cudaStream_t s[kLanes];
+  cudaEvent_t done[kLanes];
+  cudaEvent_t fork;
+  std::mutex mu;  // one forked phase at a time per device
+  bool ready = false;
+};
+
+static LanePool* lane_pool() {
+  static std::mutex mu;
+  static LanePool pools[64];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  LanePool& p = pools[dev];
+  if (!p.ready) {
+    for (int i = 0; i < kLanes; ++i) {
+      if (cudaStreamCreateWithFlags(&p.s[i], cudaStreamNonBlocking) != cudaSuccess ||
+          cudaEventCreateWithFlags(&p.done[i], cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+      }
+    }
+    if (cudaEventCreateWithFlags(&p.fork, cudaEventDisableTiming) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    p.ready = true;
+  }
+  return &p;
+}
+
+// A forked phase over n groups: lane(g) is the stream of group g; join()
+// makes the caller's stream wait for every lane used (also on error paths).
+class GroupLanes {
+ public:
+  GroupLanes(cudaStream_t main, int n) : main_(main) {
+    if (n <= 1) return;
+    pool_ = lane_pool();
+    if (!pool_) return;  // no extra streams: the groups run in order on the caller's stream
+    lock_ = std::unique_lock<std::mutex>(pool_->mu);
+    used_ = std::min(n, kLanes);
+    if (cudaEventRecord(pool_->fork, main_) != cudaSuccess) { fail(); return; }
+    for (int i = 0; i < used_; ++i)
+      if (cudaStreamWaitEvent(pool_->s[i], pool_->fork, 0) != cudaSuccess) { fail(); return; }
+  }
+  ~GroupLanes() { join(); }
+  cudaStream_t lane(int g) const { return used_ ? pool_->s[g % used_] : main_; }
+  int join() {
+    int e = 0;
+    for (int i = 0; i < used_; ++i) {
+      if (cudaEventRecord(pool_->done[i], pool_->s[i]) != cudaSuccess ||
+          cudaStreamWaitEvent(main_, pool_->done[i], 0) != cudaSuccess) {
+        e = -1;
+      }
+    }
+    used_ = 0;
+    if (lock_.owns_lock()) lock_.unlock();
+    if (e) set_error("orthogonalize: joining the group streams failed");
+    return e;
+  }
+
+ private:
+  void fail() {
+    cudaGetLastError();
+    used_ = 0;
+    if (lock_.owns_lock()) lock_.unlock();
+  }
+  cudaStream_t main_;
+  LanePool* pool_ = nullptr;
+  std::unique_lock<std::mutex> lock_;
+  int used_ = 0;
+};
+
 // Workspace of a multi-group call: six m x m buffers spanning every group's
 // matrices (so the m^3 products of all groups run as one batched GEMM), two
 // iterate buffers per group and the per-matrix scale factors.
@@ -573,21 +653,36 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     count_launch();
     if (int e = check_launch("to_half_multi")) return e;
   }
+  // runs fn(g) for every group on the group streams of one forked phase
+  auto per_group = [&](auto&& fn) -> int {
+    GroupLanes lanes(stream, ng);
+    int e = 0;
+    for (int g = 0; g < ng && !e; ++g) {
+      bg[g].st = lanes.lane(g);
+      e = fn(g);
+      bg[g].st = stream;
+    }
+    const int j = lanes.join();
+    return e ? e : j;
+  };
   int R = alloc();
-  for (int g = 0; g < ng; ++g)  // R = (s_norm / k)^2 X0 X0^T for a prescaled X0
-    if ((rc_ = syrk(bg[g], Xcur[g], pool_g(R, g), xs[g] ? xs[g] + bg[g].S : nullptr))) return rc_;
+  // R = (s_norm / k)^2 X0 X0^T for a prescaled X0
+  if ((rc_ = per_group([&](int g) { return syrk(bg[g], Xcur[g], pool_g(R, g), xs[g] ? xs[g] + bg[g].S : nullptr); })))
+    return rc_;
   int Q = -1;
   for (int t = 0; t < T; ++t) {
     const float a = coeffs[3 * t], bb = coeffs[3 * t + 1], cc = coeffs[3 * t + 2];
     if (is_reset(t)) {
       const int Rn = alloc();
-      for (int g = 0; g < ng; ++g) {
+      rc_ = per_group([&](int g) {
         uint16_t* Xn = (Xcur[g] == xa(g)) ? xb(g) : xa(g);
-        if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], epi0(Xn, 0, 0, 1.0f, xs[g], 1)))) return rc_;
-        if ((rc_ = syrk(bg[g], Xn, pool_g(Rn, g), nullptr))) return rc_;
+        int e = apply_left(bg[g], pool_g(Q, g), Xcur[g], epi0(Xn, 0, 0, 1.0f, xs[g], 1));
+        if (!e) e = syrk(bg[g], Xn, pool_g(Rn, g), nullptr);
         Xcur[g] = Xn;
         xs[g] = nullptr;
-      }
+        return e;
+      });
+      if (rc_) return rc_;
       release(Q); Q = -1;
       release(R); R = Rn;
     }
@@ -618,12 +713,11 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
     if (!p_owned_by_q) release(P);
     if (R < 0 || Q < 0) { set_error("orthogonalize: workspace pool exhausted"); return -1; }
   }
-  for (int g = 0; g < ng; ++g) {
+  return per_group([&](int g) {
     Epilogue ef = epi0(groups[g].out, 0, 0, 1.0f, xs[g], 0);  // o in bfloat16, as the reference returns it
     ef.rowsq = groups[g].rowsq;
-    if ((rc_ = apply_left(bg[g], pool_g(Q, g), Xcur[g], ef))) return rc_;
-  }
-  return 0;
+    return apply_left(bg[g], pool_g(Q, g), Xcur[g], ef);
+  });
 }
 
 int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode, const float* coeffs,
