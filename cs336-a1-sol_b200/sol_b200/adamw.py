@@ -20,12 +20,17 @@ from __future__ import annotations
 
 import ctypes as C
 
+import numpy as np
 import torch
 
 from . import _lib
 from .ema import register_optimizer
 
 MAX_GROUPS = 8
+# b2o_adamw_tensor as 64-bit words (the gradient pointer is refreshed in place each step)
+_DESC_WORDS = C.sizeof(_lib.AdamwTensor) // 8
+_GRAD_WORD = _lib.AdamwTensor.grad.offset // 8
+assert C.sizeof(_lib.AdamwTensor) % 8 == 0 and _lib.AdamwTensor.grad.offset % 8 == 0
 
 
 class AdamW(torch.optim.Optimizer):
@@ -101,8 +106,10 @@ class AdamW(torch.optim.Optimizer):
             if step_of.setdefault(gi, self._steps.get(id(p), 0)) != self._steps.get(id(p), 0):
                 raise RuntimeError("params of one group have different step counts")
             buckets.setdefault((p.device, p.dtype, st["exp_avg"].dtype), []).append((gi, p, st))
-        launches, slots, ema_idx = [], [None] * len(ps), set()
+        launches, ema_idx = [], set()
         pos = {id(p): i for i, p in enumerate(ps)}
+        # (word view of a descriptor array, its rows, the items' positions in ps, byte offsets)
+        refresh = []
         for (dev, pdt, sdt), members in buckets.items():
             descs, owners = [], []
             for gi, p, st in members:
@@ -130,14 +137,15 @@ class AdamW(torch.optim.Optimizer):
             if not descs:
                 continue
             arr = (_lib.AdamwTensor * len(descs))(*descs)
-            for i, (p, off) in enumerate(owners):
-                slots[pos[id(p)]] = (arr, i, off)
+            words = np.frombuffer(arr, dtype=np.uint64).reshape(len(descs), _DESC_WORDS)
+            refresh.append((words, np.array([pos[id(p)] for p, _ in owners]),
+                            np.array([off for _, off in owners], dtype=np.uint64)))
             launches.append((arr, len(descs), _lib.dtype_code(pdt), _lib.dtype_code(sdt), _lib.stream_ptr(dev)))
         by_group = {}
         for gi, p in zip(gis, ps):
             by_group.setdefault(gi, []).append(id(p))
         return {"key": key, "ema": self._ema, "owned": self._owned_slices, "state": self.state,
-                "keep": ps, "launches": launches, "slots": slots, "groups": by_group,
+                "keep": ps, "launches": launches, "refresh": refresh, "groups": by_group,
                 "ema_idx": frozenset(ema_idx)}
 
     @torch.no_grad()
@@ -167,10 +175,9 @@ class AdamW(torch.optim.Optimizer):
         if (plan is None or plan["key"] != key or plan["ema"] is not self._ema or plan["owned"] is not
                 self._owned_slices or plan["state"] is not self.state):
             plan = self._plan = self._build_plan(ps, gis, key)
-        for slot, g in zip(plan["slots"], gs_):
-            if slot is not None:
-                arr, i, off = slot
-                arr[i].grad = g.data_ptr() + off
+        gptr = np.fromiter((g.data_ptr() for g in gs_), dtype=np.uint64, count=len(gs_))
+        for words, where, offs in plan["refresh"]:
+            words[:, _GRAD_WORD] = gptr[where] + offs
         steps_of = {}
         for gi, ids in plan["groups"].items():
             k = self._steps.get(ids[0], 0) + 1

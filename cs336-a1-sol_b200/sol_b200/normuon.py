@@ -24,6 +24,7 @@ import ctypes as C
 import math
 from collections import OrderedDict
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -327,7 +328,8 @@ class NorMuonGNS(torch.optim.Optimizer):
     # ------------------------------------------------- cached launch plans --
     def invalidate_plan(self) -> None:
         """Drops the cached launch descriptors (rebuilt on the next step). Needed
-        only after replacing a state tensor object by hand; steps detect new
+        only after replacing a parameter's state dict or one of its state
+        tensors by hand (load_state_dict does this itself); steps detect new
         parameters, moved parameter storage, gradients appearing or vanishing,
         EMA folding and shard changes themselves."""
         self._plans = {}
@@ -344,16 +346,21 @@ class NorMuonGNS(torch.optim.Optimizer):
         batches = [(shape, ps[i:i + MAX_BATCH]) for shape, ps in by_shape.items()
                    for i in range(0, len(ps), MAX_BATCH)]
         recs = [self._prepare(ps, shape, group) for shape, ps in batches]
-        keep, slots = [], {}
+        keep = []
+        # every gradient pointer table of the plan is a slice of one flat array,
+        # refreshed each step with one vectorised write (gpos: slot of each param)
+        gflat = (C.c_void_p * max(1, len(params)))()
+        gpos_of, used = {}, 0
         front = []
         for (dev, dt), members in self._calls(recs, lambda b: (b["dev"], b["params"][0].dtype)):
             arr = (_lib.NormuonBatch * len(members))()
             for i, b in enumerate(members):
-                grads = _lib.ptr_array([None] * b["S"])
+                grads = (C.c_void_p * b["S"]).from_buffer(gflat, used * C.sizeof(C.c_void_p))
                 bufs = _lib.ptr_array([st["momentum_buffer"].data_ptr() for st in b["states"]])
                 keep += [grads, bufs]
                 for j, p in enumerate(b["params"]):
-                    slots[id(p)] = (grads, j)
+                    gpos_of[id(p)] = used + j
+                used += b["S"]
                 ws = b["ws"]
                 arr[i] = _lib.NormuonBatch(S=b["S"], r=b["r"], c=b["c"], grads=_lib.addr(grads),
                                            bufs=_lib.addr(bufs), u=ws["u"].data_ptr(),
@@ -404,16 +411,15 @@ class NorMuonGNS(torch.optim.Optimizer):
                                            vrows=_lib.addr(vrows), scratch=ws["scratch"].data_ptr())
             apply.append((arr, len(members), _lib.dtype_code(dt), _lib.stream_ptr(dev)))
         states = [self.state[p] for p in params]
-        return {"key": key, "ema": self._ema, "owned": self._owned, "keep": (keep, params, states, recs),
-                "state_ids": tuple(map(id, states)), "slots": slots, "front": front, "ortho": ortho,
-                "apply": apply, "ema_idx": frozenset(ema_idx)}
+        return {"key": key, "ema": self._ema, "owned": self._owned, "state": self.state,
+                "keep": (keep, params, states, recs, gflat), "front": front, "ortho": ortho, "apply": apply,
+                "gview": np.frombuffer(gflat, dtype=np.uint64), "gpos": np.array([gpos_of[id(p)] for p in params]),
+                "ema_idx": frozenset(ema_idx)}
 
     def _run_plan(self, plan, params, group):
         lib = _lib.load()
-        slots = plan["slots"]
-        for p in params:
-            arr, j = slots[id(p)]
-            arr[j] = p.grad.data_ptr()
+        plan["gview"][plan["gpos"]] = np.fromiter((p.grad.data_ptr() for p in params), dtype=np.uint64,
+                                                  count=len(params))
         beta = float(group["momentum"])
         nesterov = int(bool(group["nesterov"]))
         gs = self._grad_scale.data_ptr() if self._grad_scale is not None else None
@@ -478,11 +484,11 @@ class NorMuonGNS(torch.optim.Optimizer):
             # The launch descriptors depend only on which parameters step, where
             # their storage and state live, the EMA folding and the shard: cached
             # across steps; gradient pointers and scalars are filled in each step.
-            key = tuple((id(p), p.data_ptr()) for p in params)
+            key = (tuple(map(id, params)), tuple([p.data_ptr() for p in params]), len(self.state))
             pkey = (gi, id(owned))  # a sharded step alternates between its waves' owned sets
             plan = self._plans.get(pkey)
             if (plan is None or plan["key"] != key or plan["ema"] is not self._ema or plan["owned"] is not owned
-                    or plan["state_ids"] != tuple(id(self.state.get(p)) for p in params)):
+                    or plan["state"] is not self.state):
                 plan = self._plans[pkey] = self._build_plan(gi, params, group, key)
             self._run_plan(plan, params, group)
         self._grad_scale = None
