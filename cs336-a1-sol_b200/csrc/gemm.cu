@@ -23,7 +23,10 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
+#include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace b2o {
@@ -694,14 +697,62 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// rows_box: MN extent of one box for K-major operands (128 for A, 256 for B).
-static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batch, int rows_box) {
+// A tensor map is a pure function of its encode arguments (address, type,
+// dims, strides, box, swizzle, promotion), so encoded maps are kept and
+// reused: a step encodes the same ~90 maps every time it runs.
+struct MapKey {
+  uint64_t addr;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3];
+  int dtype, swizzle, promo;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    const uint64_t* w = reinterpret_cast<const uint64_t*>(&k);
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < sizeof(MapKey) / 8; ++i) h = (h ^ w[i]) * 1099511628211ull;
+    return static_cast<size_t>(h);
+  }
+};
+static_assert(sizeof(MapKey) % 8 == 0, "MapKey hashes whole words");
+
+static int encode_cached(CUtensorMap* map, CUtensorMapDataType dtype, void* addr, const cuuint64_t* dims,
+                         const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+                         CUtensorMapL2promotion promo, const char* what) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));  // padding bytes take part in the comparison
+  k.addr = reinterpret_cast<uint64_t>(addr);
+  for (int i = 0; i < 3; ++i) { k.dims[i] = dims[i]; k.box[i] = box[i]; }
+  for (int i = 0; i < 2; ++i) k.strides[i] = strides[i];
+  k.dtype = static_cast<int>(dtype); k.swizzle = static_cast<int>(swz); k.promo = static_cast<int>(promo);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(k);
+    if (it != cache.end()) { *map = it->second; return 0; }
+  }
   auto fn = encode_fn();
   if (!fn) { set_error("gemm: cuTensorMapEncodeTiled unavailable"); return -1; }
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, addr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, promo,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(std::string("gemm: ") + what + " tensor map failed with code " + std::to_string(static_cast<int>(r)));
+    return -1;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() >= 8192) cache.clear();
+  cache.emplace(k, *map);
+  return 0;
+}
+
+// rows_box: MN extent of one box for K-major operands (128 for A, 256 for B).
+static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batch, int rows_box) {
   cuuint64_t dims[3];
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld) * 2, static_cast<cuuint64_t>(op.stride) * 2};
   cuuint32_t box[3];
-  cuuint32_t estr[3] = {1, 1, 1};
   if (op.kmajor) {
     dims[0] = K; dims[1] = mn; box[0] = BK; box[1] = rows_box;
   } else {
@@ -709,33 +760,19 @@ static int make_map(CUtensorMap* map, const Operand& op, int mn, int K, int batc
   }
   dims[2] = batch; box[2] = 1;
   if (batch == 1) strides[1] = strides[0] * dims[1];  // any valid stride
-  CUresult r = fn(map, op.half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(op.ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("gemm: cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
-    return -1;
-  }
-  return 0;
+  return encode_cached(map, op.half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                       const_cast<uint16_t*>(op.ptr), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "operand");
 }
 
 // Output map: rows of D (ldd apart) x columns, 32 x 32 boxes, 64-byte swizzle.
 static int make_store_map(CUtensorMap* map, const Epilogue& E, int M, int N, int batch) {
-  auto fn = encode_fn();
-  if (!fn) { set_error("gemm: cuTensorMapEncodeTiled unavailable"); return -1; }
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(E.ldd) * 2, static_cast<cuuint64_t>(E.strideD) * 2};
   if (batch == 1) strides[1] = strides[0] * dims[1];
   cuuint32_t box[3] = {32, 32, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, E.d_half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, E.D, dims,
-                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("gemm: output tensor map failed with code " + std::to_string(static_cast<int>(r)));
-    return -1;
-  }
-  return 0;
+  return encode_cached(map, E.d_half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, E.D, dims,
+                       strides, box, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, "output");
 }
 
 }  // namespace tc
