@@ -724,7 +724,8 @@ def main():
     ap.add_argument("--exchange", default="auto", choices=["auto", "ce", "hybrid", "nccl"],
                     help="N>1: copy-engine pushes over CUDA IPC mappings, NCCL all-gathers, or both")
     ap.add_argument("--push-streams", type=int, default=1, help="N>1: streams the copy-engine pushes use")
-    ap.add_argument("--waves", type=int, default=1, help="N>1: NorMuon waves per rank (exchange overlaps compute)")
+    ap.add_argument("--waves", type=int, default=None,
+                    help="N>1: NorMuon waves per rank (exchange overlaps compute); default 1 on 2 GPUs, 2 from 4")
     ap.add_argument("--assignment", default="lpt", choices=["lpt", "runs"], help="N>1: matrix-to-rank assignment")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -165,7 +165,7 @@ def split_waves(shapes, waves: int):
 
 class ShardedStep:
     def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024,
-                 exchange: str = "auto", push_streams: int = 1, waves: int = 1, assignment: str = "lpt"):
+                 exchange: str = "auto", push_streams: int = 1, waves: int | None = None, assignment: str = "lpt"):
         """exchange: "ce" (copy-engine pushes of the tables and the arena),
         "hybrid" (copy-engine pushes of the tables, overlapped with NorMuon;
         NCCL all-gather of the arena), "nccl" (all-gathers only) or "auto".
@@ -176,7 +176,9 @@ class ShardedStep:
         waves: each rank steps its NorMuon matrices in this many waves and
         starts exchanging a wave's weights as soon as that wave is applied, so
         the exchange overlaps the next wave's compute (the arena is laid out
-        wave by wave, each wave rank by rank).
+        wave by wave, each wave rank by rank). None: one wave on two ranks,
+        two from four ranks on (measured on 4 x B200, L14 step: 1.77 ms with
+        two waves against 1.87 with one; equal on two ranks).
         assignment: "lpt" or "runs" (see assign_matrices)."""
         if exchange not in ("auto", "ce", "hybrid", "nccl"):
             raise ValueError("exchange must be 'auto', 'ce', 'hybrid' or 'nccl'")
@@ -197,7 +199,7 @@ class ShardedStep:
         muon._owned = {id(p) for p, k in zip(mparams, owner) if k == rank}
         self.owned_all = muon._owned
         # every rank's matrices split into the same number of waves
-        self.waves = max(1, int(waves))
+        self.waves = max(1, int(waves)) if waves is not None else (1 if world <= 2 else 2)
         per_rank = [[p for p, k in zip(mparams, owner) if k == r] for r in range(world)]
         wave_of = {}
         for r, ps in enumerate(per_rank):
