@@ -7,10 +7,14 @@ engine arm (default): the L14/d1024/d_ff 5632/V 32768 recipe parameter set
 on seeded synthetic bf16 tensors resident in HBM; one
 step = muon.step(); adamw.step(); ema.update() through the drop-in API
 (build_optimizers + EmaWeights). Prints one JSON line with the step time, the
-Gram Newton-Schulz GEMM roofline, the end-to-end time through the same API
-with host gradients copied in and a result read back, and the CPU baseline.
-With N > 1 (torchrun), the step is sharded by matrices / table rows and the
-updated bf16 weights are all-gathered with NCCL; time = max over ranks.
+Gram Newton-Schulz GEMM roofline (denominator chosen from the clocks of the
+run it is measured in), the end-to-end time through the same API with host
+gradients copied in and a result read back; at N = 1 also the configs[2] /
+configs[3] micro-benchmarks, the reference's step run by torch on the same
+GPU and the CPU baseline. With N > 1 (torchrun), the step is sharded by
+matrices / table rows, the updated bf16 weights are exchanged over NVLink
+(copy-engine pushes and NCCL), time = max over ranks, and the line carries a
+bitwise comparison of every rank's results with the unsharded engine.
 
 reference arm: the reference's own optimizer math (the CPU oracle, bit-exact
 with transformer_lm.sol_modules on CPU) on the host cores, on a 1/14 sample of

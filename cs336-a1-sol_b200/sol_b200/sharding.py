@@ -333,11 +333,13 @@ class ShardedStep:
         # ctypes argument arrays built once: the pushes reuse them every step
         self._plans = {k: [_lib.copy_args(c) if c else None for c in per_stream] for k, per_stream in plans.items()}
         self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            self._push_ev = torch.cuda.Event()
         self.exchange = self._requested
 
     def _push(self, which):
         cur = torch.cuda.current_stream()
-        ev = torch.cuda.Event()
+        ev = self._push_ev  # reused: each wait takes the event as recorded at that moment
         ev.record(cur)
         for st, args in zip(self._streams, self._plans[which]):
             if args is not None:
