@@ -302,8 +302,8 @@ def engine_arm(args, world, rank, local):
                                    adam_master="bf16_mt", **RECIPE)
     ema = EmaWeights(model, 0.999)
     sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, exchange=args.exchange,
-                          push_streams=args.push_streams, waves=args.waves,
-                          assignment=args.assignment) if world > 1 else None
+                          push_streams=args.push_streams, waves=args.waves, assignment=args.assignment,
+                          adamw_between_waves=args.adamw_between_waves) if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     ortho_events = []
     adam_ev = []
@@ -441,6 +441,7 @@ def engine_arm(args, world, rank, local):
                    "exchange": sharded.exchange if sharded is not None else None,
                    "push_streams": sharded.push_streams if sharded is not None else None,
                    "waves": sharded.waves if sharded is not None else None,
+                   "adamw_between_waves": sharded.adamw_between_waves if sharded is not None else None,
                    "assignment": sharded.assignment if sharded is not None else None},
         "phases_ms": {"orthogonalize": ortho_ms, "adamw": adam_ms,
                       "normuon_other+ema+gather": ms_local - ortho_ms - adam_ms},
@@ -515,7 +516,8 @@ def sharded_parity(args, cfg, world, rank, dev, steps=3):
     muon, adamw = build_optimizers(model, **kw)
     ema = EmaWeights(model, 0.999)
     sh = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, exchange=args.exchange,
-                     push_streams=args.push_streams, waves=args.waves, assignment=args.assignment)
+                     push_streams=args.push_streams, waves=args.waves, assignment=args.assignment,
+                     adamw_between_waves=args.adamw_between_waves)
     ref = synth.SyntheticLM(cfg, device=dev, seed=0)
     rmuon, radamw = build_optimizers(ref, **kw)
     rema = EmaWeights(ref, 0.999)
@@ -587,7 +589,10 @@ def e2e_leg(args, model, muon, adamw, ema, sharded, flat_grad, one_step, world, 
         return merged
 
     ranges = {k: merge(v) for k, v in ranges.items()}
-    order = ["adamw", "normuon"] if sharded is not None else ["normuon", "adamw"]
+    if sharded is not None:
+        order = [sharded.first_optimizer, "normuon" if sharded.first_optimizer == "adamw" else "adamw"]
+    else:
+        order = ["normuon", "adamw"]
     h2d = sum(n for v in ranges.values() for _, n in v) * host.element_size()
     probe = next(iter(muon.param_groups[0]["params"]))
     out = torch.empty(256, dtype=probe.dtype, pin_memory=True)
@@ -731,6 +736,8 @@ def main():
     ap.add_argument("--waves", type=int, default=None,
                     help="N>1: NorMuon waves per rank (exchange overlaps compute); default 1 on 2 GPUs, 2 from 4")
     ap.add_argument("--assignment", default="lpt", choices=["lpt", "runs"], help="N>1: matrix-to-rank assignment")
+    ap.add_argument("--adamw-between-waves", action="store_true",
+                    help="N>1 with two or more waves: AdamW after the first NorMuon wave")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-micro", action="store_true", help="N=1: skip the configs[2]/[3] micro-benchmarks")

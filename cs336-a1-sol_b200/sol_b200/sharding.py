@@ -165,7 +165,8 @@ def split_waves(shapes, waves: int):
 
 class ShardedStep:
     def __init__(self, model, muon, adamw, ema, world: int, rank: int, group=None, min_rows_shard: int = 1024,
-                 exchange: str = "auto", push_streams: int = 1, waves: int | None = None, assignment: str = "lpt"):
+                 exchange: str = "auto", push_streams: int = 1, waves: int | None = None, assignment: str = "lpt",
+                 adamw_between_waves: bool = False):
         """exchange: "ce" (copy-engine pushes of the tables and the arena),
         "hybrid" (copy-engine pushes of the tables, overlapped with NorMuon;
         NCCL all-gather of the arena), "nccl" (all-gathers only) or "auto".
@@ -179,7 +180,11 @@ class ShardedStep:
         wave by wave, each wave rank by rank). None: one wave on two ranks,
         two from four ranks on (measured on 4 x B200, L14 step: 1.77 ms with
         two waves against 1.87 with one; equal on two ranks).
-        assignment: "lpt" or "runs" (see assign_matrices)."""
+        assignment: "lpt" or "runs" (see assign_matrices).
+        adamw_between_waves: with two or more waves, run AdamW after the first
+        NorMuon wave instead of before NorMuon, so the first wave's exchange
+        also overlaps AdamW (the tables are then exchanged while the later
+        waves compute)."""
         if exchange not in ("auto", "ce", "hybrid", "nccl"):
             raise ValueError("exchange must be 'auto', 'ce', 'hybrid' or 'nccl'")
         required = exchange != "auto"
@@ -200,6 +205,9 @@ class ShardedStep:
         self.owned_all = muon._owned
         # every rank's matrices split into the same number of waves
         self.waves = max(1, int(waves)) if waves is not None else (1 if world <= 2 else 2)
+        self.adamw_between_waves = bool(adamw_between_waves) and self.waves > 1
+        # which optimizer reads its gradients first in step() (callers streaming gradients in)
+        self.first_optimizer = "normuon" if self.adamw_between_waves else "adamw"
         per_rank = [[p for p, k in zip(mparams, owner) if k == r] for r in range(world)]
         wave_of = {}
         for r, ps in enumerate(per_rank):
@@ -411,14 +419,19 @@ class ShardedStep:
         mark = mark or (lambda name: None)
         before = before or (lambda name: None)
         push_tables = self.exchange in ("ce", "hybrid")
-        before("adamw")
-        self.adamw.step()
-        mark("adamw")
         works = []
-        if push_tables:
-            self._push("tables")
-        elif self.world > 1:
-            works = self._gather_tables(async_op=True)
+
+        def adamw_and_tables():
+            before("adamw")
+            self.adamw.step()
+            mark("adamw")
+            if push_tables:
+                self._push("tables")
+            elif self.world > 1:
+                works.extend(self._gather_tables(async_op=True))
+
+        if not self.adamw_between_waves:
+            adamw_and_tables()
         before("normuon")
         arena_works = []
         try:
@@ -432,6 +445,9 @@ class ShardedStep:
                         x = self._gather_arena_wave(w, async_op=True)
                         if x is not None:
                             arena_works.append(x)
+                if w == 0 and self.adamw_between_waves:
+                    self.muon._owned = self.owned_all
+                    adamw_and_tables()
         finally:
             self.muon._owned = self.owned_all
         mark("normuon")

@@ -27,7 +27,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, exchange, q, dp=False, waves=1, assignment="lpt"):
+def _worker(rank, world, port, exchange, q, dp=False, waves=1, assignment="lpt", between=False):
     import torch.distributed as dist
 
     from sol_b200 import EmaWeights, build_optimizers, synth
@@ -46,7 +46,7 @@ def _worker(rank, world, port, exchange, q, dp=False, waves=1, assignment="lpt")
         muon, adamw = build_optimizers(model, adam_master="bf16_mt", **KW)
         ema = EmaWeights(model, 0.999)
         sharded = ShardedStep(model, muon, adamw, ema, world=world, rank=rank, min_rows_shard=16,
-                              exchange=exchange, waves=waves, assignment=assignment)
+                              exchange=exchange, waves=waves, assignment=assignment, adamw_between_waves=between)
         ref = synth.SyntheticLM(cfg, device=dev, seed=0)
         rmuon, radamw = build_optimizers(ref, adam_master="bf16_mt", **KW)
         rema = EmaWeights(ref, 0.999)
@@ -100,10 +100,11 @@ def _worker(rank, world, port, exchange, q, dp=False, waves=1, assignment="lpt")
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange,dp,waves,assignment", [
-    ("ce", False, 1, "lpt"), ("hybrid", False, 1, "lpt"), ("nccl", False, 1, "lpt"), ("auto", True, 1, "lpt"),
-    ("ce", False, 2, "runs"), ("hybrid", False, 2, "lpt"), ("nccl", True, 2, "runs")])
-def test_sharded_step_bit_identical_to_single_gpu(exchange, dp, waves, assignment):
+@pytest.mark.parametrize("exchange,dp,waves,assignment,between", [
+    ("ce", False, 1, "lpt", False), ("hybrid", False, 1, "lpt", False), ("nccl", False, 1, "lpt", False),
+    ("auto", True, 1, "lpt", False), ("ce", False, 2, "runs", False), ("hybrid", False, 2, "lpt", False),
+    ("nccl", True, 2, "runs", False), ("hybrid", False, 2, "lpt", True), ("ce", False, 2, "lpt", True)])
+def test_sharded_step_bit_identical_to_single_gpu(exchange, dp, waves, assignment, between):
     """dp: each rank steps on its own gradients after reduce_gradients; the
     single-GPU reference steps on their mean. waves > 1: each wave's weights
     are exchanged while the next wave computes."""
@@ -113,7 +114,7 @@ def test_sharded_step_bit_identical_to_single_gpu(exchange, dp, waves, assignmen
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q, dp, waves, assignment))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q, dp, waves, assignment, between))
              for r in range(world)]
     for p in procs:
         p.start()
