@@ -177,9 +177,8 @@ class ShardedStep:
         waves: each rank steps its NorMuon matrices in this many waves and
         starts exchanging a wave's weights as soon as that wave is applied, so
         the exchange overlaps the next wave's compute (the arena is laid out
-        wave by wave, each wave rank by rank). None: one wave on two ranks,
-        two from four ranks on (measured on 4 x B200, L14 step: 1.77 ms with
-        two waves against 1.87 with one; equal on two ranks).
+        wave by wave, each wave rank by rank). None: two waves from four ranks
+        on where each rank holds at least 16 NorMuon matrices, else one.
         assignment: "lpt" or "runs" (see assign_matrices).
         adamw_between_waves: with two or more waves, run AdamW after the first
         NorMuon wave instead of before NorMuon, so the first wave's exchange
@@ -204,7 +203,13 @@ class ShardedStep:
         muon._owned = {id(p) for p, k in zip(mparams, owner) if k == rank}
         self.owned_all = muon._owned
         # every rank's matrices split into the same number of waves
-        self.waves = max(1, int(waves)) if waves is not None else (1 if world <= 2 else 2)
+        if waves is None:
+            # two waves only where each rank keeps batches large enough to fill
+            # the GEMMs (measured, L14 step: 4 ranks / ~18 matrices each, 1.77
+            # ms with two waves against 1.87; 8 ranks / ~9 each, 1.77 against
+            # 1.57; 2 ranks, equal)
+            waves = 2 if world > 2 and len(mparams) / world >= 16 else 1
+        self.waves = max(1, int(waves))
         self.adamw_between_waves = bool(adamw_between_waves) and self.waves > 1
         # which optimizer reads its gradients first in step() (callers streaming gradients in)
         self.first_optimizer = "normuon" if self.adamw_between_waves else "adamw"
@@ -459,10 +464,15 @@ class ShardedStep:
             # landed, so its completion means every rank's pushes did
             dist.all_reduce(self._flag, group=self.group)
         elif self.world > 1:
+            last = self._gather_arena_wave(self.waves - 1, async_op=True)
             if push_tables:
-                self._join_pushes()  # the last all-gather is then also the pushes' barrier
-            self._gather_arena_wave(self.waves - 1)
-            for x in arena_works:
+                # the last all-gather crosses NVLink together with the table
+                # pushes still in flight; a one-element all-reduce, entered by
+                # every rank after its own pushes landed and ordered after the
+                # all-gathers on NCCL's stream, completes when both have
+                self._join_pushes()
+                dist.all_reduce(self._flag, group=self.group)
+            for x in arena_works + ([last] if last is not None else []):
                 x.wait()
         mark("arena_gather")
         for x in works:
