@@ -734,7 +734,7 @@ def main():
                     help="N>1: copy-engine pushes over CUDA IPC mappings, NCCL all-gathers, or both")
     ap.add_argument("--push-streams", type=int, default=1, help="N>1: streams the copy-engine pushes use")
     ap.add_argument("--waves", type=int, default=None,
-                    help="N>1: NorMuon waves per rank (exchange overlaps compute); default 1 on 2 GPUs, 2 from 4")
+                    help="N>1: NorMuon waves per rank (exchange overlaps compute); default 2 from 4 GPUs with at least 16 matrices per rank, else 1")
     ap.add_argument("--assignment", default="lpt", choices=["lpt", "runs"], help="N>1: matrix-to-rank assignment")
     ap.add_argument("--adamw-between-waves", action="store_true",
                     help="N>1 with two or more waves: AdamW after the first NorMuon wave")
