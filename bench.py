@@ -457,7 +457,8 @@ def engine_arm(args, world, rank, local):
                      "launches_per_step": gemm_n, "gemm_ms_per_step": gemm_ms, "flops_per_step": gemm_flops,
                      "flops_per_launch": gemm_flops / max(1, gemm_n),
                      "timing": "CUDA events on the launching stream around the orthogonaliser calls of the "
-                               "tensor-core classes (30 GEMM launches each, nothing else), second timed run",
+                               "tensor-core classes (30 GEMM launches each, nothing else; replayed from a "
+                               "launch graph), second timed run",
                      "peak_kind": peak_label,
                      "frac_of_burst_peak": (achieved / peak_burst) if achieved else None,
                      "frac_of_sustained_peak": (achieved / peak_sus) if achieved else None,
@@ -467,6 +468,7 @@ def engine_arm(args, world, rank, local):
                            "tflops": flops / (ortho_ms * 1e-3) / 1e12 if ortho_ms > 0 else None},
         "host_enqueue_ms_per_step": host_t * 1e3 / args.steps,
         "clocks": clocks, "gpu_launches": launches,
+        "launch_graphs": _lib.launch_graph_stats(),
     }
     if e2e:
         line["e2e"] = e2e

@@ -16,8 +16,14 @@ namespace b2o {
 // Host-side error text for the last failing call on this thread.
 void set_error(const std::string& msg);
 // Counts kernel launches made by the library (reported by the benchmark).
+// While this thread captures a launch graph, launches are counted into
+// *t_capture_launches instead (they run only when the graph is replayed).
 extern std::atomic<int64_t> g_launches;
-inline void count_launch(int n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+extern thread_local int64_t* t_capture_launches;
+inline void count_launch(int n = 1) {
+  if (t_capture_launches) *t_capture_launches += n;
+  else g_launches.fetch_add(n, std::memory_order_relaxed);
+}
 
 // Device error word (one per device, lazily allocated by the library at load
 // of the first device call; see c_abi.cu). Kernels OR error bits into it.

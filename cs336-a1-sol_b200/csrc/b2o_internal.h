@@ -99,6 +99,12 @@ int64_t ortho_workspace_bytes_multi(const OrthoGroup* g, int ng);
 int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float* coeffs, int T, const int* resets,
                         int nresets, float norm_eps, float norm_safety, void* ws, int64_t ws_bytes,
                         cudaStream_t stream);
+// orthogonalize_multi through the launch-graph cache (what the C ABI calls).
+int orthogonalize_multi_cached(const OrthoGroup* groups, int ng, int mode, const float* coeffs, int T,
+                               const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
+                               int64_t ws_bytes, cudaStream_t stream);
+int set_launch_graphs(int enable);  // returns the previous setting
+void launch_graph_stats(int64_t* captures, int64_t* replays, int64_t* failures);
 int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode,
                   const float* coeffs, int T, const int* resets, int nresets, float norm_eps,
                   float norm_safety, void* ws, int64_t ws_bytes, uint16_t* out, float* rowsq,

@@ -12,6 +12,7 @@
 namespace b2o {
 
 std::atomic<int64_t> g_launches{0};
+thread_local int64_t* t_capture_launches = nullptr;
 static thread_local std::string t_last_error;
 
 void set_error(const std::string& msg) { t_last_error = msg; }
@@ -85,6 +86,13 @@ int b2o_last_error(char* buf, int buflen) {
 int64_t b2o_launch_count(void) { return g_launches.load(); }
 
 int b2o_num_sms(void) { return num_sms(); }
+
+int b2o_launch_graphs(int enable) { return set_launch_graphs(enable); }
+
+int b2o_launch_graph_stats(int64_t* captures, int64_t* replays, int64_t* failures) {
+  launch_graph_stats(captures, replays, failures);
+  return 0;
+}
 
 int b2o_gemm_timing(int enable) {
   GemmTimer::instance().enabled = enable != 0;
@@ -165,8 +173,8 @@ int b2o_orthogonalize_multi(const b2o_ortho_group* groups, int ngroups, int mode
                             int64_t ws_bytes, void* stream) {
   if (!groups || ngroups <= 0) { set_error("orthogonalize: no groups"); return -1; }
   auto v = to_groups(groups, ngroups);
-  return orthogonalize_multi(v.data(), ngroups, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, d_ws,
-                             ws_bytes, static_cast<cudaStream_t>(stream));
+  return orthogonalize_multi_cached(v.data(), ngroups, mode, coeffs, T, resets, nresets, norm_eps, norm_safety,
+                                    d_ws, ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int64_t b2o_normuon_apply_scratch_floats(int S, int r) {

@@ -28,9 +28,12 @@
 #include "b2o_internal.h"
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 namespace b2o {
@@ -720,11 +723,170 @@ int orthogonalize_multi(const OrthoGroup* groups, int ng, int mode, const float*
   });
 }
 
+// ---------------------------------------------------------------------------
+// Launch graphs of repeated calls. An optimizer step calls the orthogonaliser
+// with the same workspaces, groups, coefficients and restarts every step, and
+// a call's launches (about 30 GEMMs for an L14 step, each encoding tensor maps
+// and launching from the host) depend on nothing else. So the second call
+// with a given argument set is captured into a CUDA graph (on a private
+// stream, with the group streams forked and joined inside it, programmatic
+// dependent launches kept as programmatic edges) and every later one replays
+// it with a single launch on the caller's stream. The first call runs the
+// launches directly: it validates the arguments and performs the one-time
+// setup (shared-memory opt-ins, stream pool, tensor-map cache) outside any
+// capture. Replay runs exactly the kernels, arguments and order a direct call
+// would; a capture that fails marks its key for direct launches.
+namespace {
+struct OrthoGraph {
+  cudaGraphExec_t exec = nullptr;
+  int64_t launches = 0;  // kernels one replay launches
+  bool seen = false;     // one direct call with these arguments succeeded
+  bool failed = false;   // capture or instantiation failed: direct launches
+};
+struct GraphCache {
+  std::mutex mu;
+  std::unordered_map<std::string, OrthoGraph> map;
+  cudaStream_t cap[64] = {};
+  int64_t captures = 0, replays = 0, failures = 0;
+};
+GraphCache& graph_cache() {
+  static GraphCache c;
+  return c;
+}
+std::atomic<int> g_graphs_on{-1};
+constexpr size_t kMaxGraphs = 256;
+
+bool graphs_on() {
+  int v = g_graphs_on.load();
+  if (v < 0) {
+    const char* e = std::getenv("B2O_GRAPHS");
+    v = (e && e[0] == '0') ? 0 : 1;
+    g_graphs_on.store(v);
+  }
+  return v != 0;
+}
+
+template <typename T>
+void put(std::string& k, const T& v) { k.append(reinterpret_cast<const char*>(&v), sizeof(T)); }
+}  // namespace
+
+int set_launch_graphs(int enable) {
+  const int prev = graphs_on() ? 1 : 0;
+  g_graphs_on.store(enable ? 1 : 0);
+  return prev;
+}
+
+void launch_graph_stats(int64_t* captures, int64_t* replays, int64_t* failures) {
+  GraphCache& gc = graph_cache();
+  std::lock_guard<std::mutex> lk(gc.mu);
+  if (captures) *captures = gc.captures;
+  if (replays) *replays = gc.replays;
+  if (failures) *failures = gc.failures;
+}
+
+int orthogonalize_multi_cached(const OrthoGroup* groups, int ng, int mode, const float* coeffs, int T,
+                               const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
+                               int64_t ws_bytes, cudaStream_t stream) {
+  auto direct = [&](cudaStream_t st) {
+    return orthogonalize_multi(groups, ng, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, ws, ws_bytes,
+                               st);
+  };
+  // direct launches: graphs off, GEMM timing on (events per launch), arguments
+  // the direct path rejects, or a caller that is capturing its own graph
+  if (!graphs_on() || GemmTimer::instance().enabled || ng <= 0 || ng > 4096 || !groups || !coeffs || T < 1 ||
+      T > 64 || nresets < 0 || nresets > 64 || (nresets > 0 && !resets))
+    return direct(stream);
+  cudaStreamCaptureStatus cst = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cst) != cudaSuccess) { cudaGetLastError(); return direct(stream); }
+  if (cst != cudaStreamCaptureStatusNone) return direct(stream);
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { cudaGetLastError(); return direct(stream); }
+
+  std::string key;
+  key.reserve(96 + 56 * static_cast<size_t>(ng) + 12 * T);
+  put(key, dev); put(key, mode); put(key, T); put(key, nresets); put(key, norm_eps); put(key, norm_safety);
+  put(key, ws); put(key, ws_bytes); put(key, ng);
+  for (int i = 0; i < ng; ++i) {
+    const OrthoGroup& g = groups[i];
+    put(key, g.U); put(key, g.partial); put(key, g.out); put(key, g.rowsq);
+    put(key, g.S); put(key, g.r); put(key, g.c); put(key, g.xscale);
+  }
+  key.append(reinterpret_cast<const char*>(coeffs), sizeof(float) * 3 * static_cast<size_t>(T));
+  if (nresets > 0) key.append(reinterpret_cast<const char*>(resets), sizeof(int) * static_cast<size_t>(nresets));
+
+  GraphCache& gc = graph_cache();
+  std::unique_lock<std::mutex> lk(gc.mu);
+  auto it = gc.map.find(key);
+  if (it == gc.map.end()) {
+    if (gc.map.size() >= kMaxGraphs) {  // argument sets keep changing: start over (in-flight replays finish)
+      for (auto& kv : gc.map)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+      gc.map.clear();
+    }
+    lk.unlock();
+    const int rc = direct(stream);
+    if (rc == 0) {
+      lk.lock();
+      gc.map[key].seen = true;
+    }
+    return rc;
+  }
+  OrthoGraph& e = it->second;
+  if (e.failed) { lk.unlock(); return direct(stream); }
+  if (!e.exec) {
+    if (!gc.cap[dev] && cudaStreamCreateWithFlags(&gc.cap[dev], cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      gc.cap[dev] = nullptr;
+      e.failed = true;
+      ++gc.failures;
+      lk.unlock();
+      return direct(stream);
+    }
+    int64_t counted = 0;
+    t_capture_launches = &counted;
+    cudaGraph_t graph = nullptr;
+    cudaError_t ce = cudaStreamBeginCapture(gc.cap[dev], cudaStreamCaptureModeThreadLocal);
+    int rc = -1;
+    if (ce == cudaSuccess) {
+      rc = direct(gc.cap[dev]);
+      ce = cudaStreamEndCapture(gc.cap[dev], &graph);
+    }
+    t_capture_launches = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (rc == 0 && ce == cudaSuccess && graph) ce = cudaGraphInstantiateWithFlags(&exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (rc != 0 || ce != cudaSuccess || !exec) {
+      cudaGetLastError();
+      if (exec) cudaGraphExecDestroy(exec);
+      e.failed = true;
+      ++gc.failures;
+      lk.unlock();
+      return direct(stream);
+    }
+    e.exec = exec;
+    e.launches = counted;
+    ++gc.captures;
+  }
+  cudaGraphExec_t exec = e.exec;
+  const int64_t n = e.launches;
+  ++gc.replays;
+  lk.unlock();
+  const cudaError_t le = cudaGraphLaunch(exec, stream);
+  if (le != cudaSuccess) {
+    set_error(std::string("orthogonalize: graph launch: ") + cudaGetErrorString(le));
+    cudaGetLastError();
+    return static_cast<int>(le);
+  }
+  count_launch(static_cast<int>(n));
+  return 0;
+}
+
 int orthogonalize(const uint16_t* U, const float* partial, int S, int r, int c, int mode, const float* coeffs,
                   int T, const int* resets, int nresets, float norm_eps, float norm_safety, void* ws,
                   int64_t ws_bytes, uint16_t* out, float* rowsq, cudaStream_t stream) {
   OrthoGroup g{U, partial, out, rowsq, S, r, c};
-  return orthogonalize_multi(&g, 1, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, ws, ws_bytes, stream);
+  return orthogonalize_multi_cached(&g, 1, mode, coeffs, T, resets, nresets, norm_eps, norm_safety, ws, ws_bytes,
+                                    stream);
 }
 
 }  // namespace b2o

@@ -100,6 +100,8 @@ SIGNATURES = {
     "b2o_launch_count": (c_int64, []),
     "b2o_check_device_error": (c_int, [c_void_p]),
     "b2o_num_sms": (c_int, []),
+    "b2o_launch_graphs": (c_int, [c_int]),
+    "b2o_launch_graph_stats": (c_int, [C.POINTER(c_int64), C.POINTER(c_int64), C.POINTER(c_int64)]),
     "b2o_gemm_timing": (c_int, [c_int]),
     "b2o_gemm_timing_read": (c_int, [C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(c_int64)]),
     "b2o_adamw_step": (c_int, [C.POINTER(AdamwTensor), c_int, C.POINTER(AdamwGroup), c_int, c_int, c_int,
@@ -223,6 +225,18 @@ def device_error(stream: int | None = None) -> int:
     """Synchronises the stream and returns/clears the device error word."""
     lib = load()
     return int(lib.b2o_check_device_error(stream if stream is not None else stream_ptr()))
+
+
+def launch_graphs(enable: bool) -> bool:
+    """Turns the orthogonaliser's launch graphs on or off; returns the previous setting."""
+    return bool(load().b2o_launch_graphs(1 if enable else 0))
+
+
+def launch_graph_stats() -> dict:
+    """Launch graphs captured, replayed and failed (failed argument sets launch directly)."""
+    c, r, f = c_int64(), c_int64(), c_int64()
+    load().b2o_launch_graph_stats(C.byref(c), C.byref(r), C.byref(f))
+    return {"captures": c.value, "replays": r.value, "failures": f.value}
 
 
 def gemm_timing(enable: bool) -> None:

@@ -50,6 +50,15 @@ int b2o_num_sms(void);
  * b2o_gemm_timing_read synchronises on them and returns the summed device
  * time, the launches' algorithmic FLOPs (symmetric outputs at half) and the
  * number of launches since the previous read. */
+/* Launch graphs (no reference counterpart): the second orthogonaliser call
+ * with a given argument set is captured into a CUDA graph and later calls with
+ * the same arguments replay it (same kernels, arguments and order; one host
+ * launch instead of ~30). b2o_launch_graphs(0) turns this off (as does
+ * B2O_GRAPHS=0 in the environment) and returns the previous setting;
+ * b2o_launch_graph_stats reports graphs captured, replays and failed captures
+ * (whose argument sets then launch directly). */
+int b2o_launch_graphs(int enable);
+int b2o_launch_graph_stats(int64_t* captures, int64_t* replays, int64_t* failures);
 int b2o_gemm_timing(int enable);
 int b2o_gemm_timing_read(double* ms, double* flops, int64_t* launches);
 
