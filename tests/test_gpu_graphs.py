@@ -105,3 +105,36 @@ def test_changed_workspace_gets_its_own_graph(cuda):
         _lib.launch_graphs(prev)
     assert _lib.device_error() == 0
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_changed_iteration_count_captures_new_graphs(cuda):
+    """ns_steps changed between steps (a different coefficient table and
+    restart list) is a new argument set: it launches directly once, is
+    captured, and the results equal direct launches throughout."""
+    def run(graphs):
+        g = torch.Generator(device=cuda).manual_seed(9)
+        params = [torch.nn.Parameter((torch.randn(s, generator=g, device=cuda) * 0.02).to(torch.bfloat16))
+                  for s in SHAPES]
+        opt = NorMuonGNS(params, lr=8e-3, weight_decay=0.1, cautious_wd=True, bf16_master=True)
+        prev = _lib.launch_graphs(graphs)
+        try:
+            for k in range(6):
+                opt.param_groups[0]["ns_steps"] = 5 if k < 3 else 3
+                for p in params:
+                    p.grad = (torch.randn(p.shape, generator=g, device=cuda) * 1e-3).to(torch.bfloat16)
+                opt.step()
+            torch.cuda.synchronize()
+        finally:
+            _lib.launch_graphs(prev)
+        assert _lib.device_error() == 0
+        return [p.detach().clone() for p in params]
+
+    direct = run(False)
+    s0 = _lib.launch_graph_stats()
+    graphed = run(True)
+    s1 = _lib.launch_graph_stats()
+    assert s1["failures"] == s0["failures"]
+    assert s1["captures"] - s0["captures"] == 6  # three m-classes x two iteration counts
+    assert s1["replays"] - s0["replays"] == 12
+    for i, (a, b) in enumerate(zip(direct, graphed)):
+        assert torch.equal(a, b), f"parameter {i} differs under graph replay"
