@@ -170,7 +170,7 @@ class ShardedStep:
         """exchange: "ce" (copy-engine pushes of the tables and the arena),
         "hybrid" (copy-engine pushes of the tables, overlapped with NorMuon;
         NCCL all-gather of the arena), "nccl" (all-gathers only) or "auto"
-        ("ce" up to four ranks, "hybrid" above).
+        ("ce" where every rank can export its buffers).
         Copy-engine modes fall back to NCCL where a rank cannot export its
         buffers ("auto") or raise. push_streams: streams the pushes are spread
         over; peers are visited in ring order rank+1, rank+2, ... so with one
@@ -191,13 +191,11 @@ class ShardedStep:
             raise ValueError("exchange must be 'auto', 'ce', 'hybrid' or 'nccl'")
         required = exchange != "auto"
         if exchange == "auto":
-            # measured (L14 step): up to four ranks copy-engine pushes of the
-            # arena win (4 ranks, two waves: 1.50 against 1.77 ms, because the
-            # first wave's NCCL all-gather takes SMs from the second wave's
-            # GEMMs, 597 against 741 TFLOP/s); on eight ranks (one wave) NCCL's
-            # all-gather of the arena was faster than pushes to seven peers, and
-            # the table pushes stay on the copy engines (no SMs taken)
-            exchange = "ce" if world <= 4 else "hybrid"
+            # measured (L14 step): copy-engine pushes of the arena win at every
+            # size (4 ranks, two waves: 1.50 against 1.77 ms, because a wave's
+            # NCCL all-gather takes SMs from the next wave's GEMMs, 597 against
+            # 741 TFLOP/s; 8 ranks, one wave: 1.52 against 1.58 ms)
+            exchange = "ce"
         self.world, self.rank, self.group = world, rank, group
         self.push_streams = max(1, min(int(push_streams), max(1, world - 1)))
         self.muon, self.adamw, self.ema = muon, adamw, ema
